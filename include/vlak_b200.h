@@ -1,0 +1,144 @@
+/*
+ * vlak_b200.h -- C ABI of the B200 (sm_100a) kernels that sit behind the
+ * torch.ops.vlak operators.
+ *
+ * Every entry point takes plain device pointers, sizes, element strides and a
+ * CUDA stream handle (a cudaStream_t passed as void*; NULL = legacy default
+ * stream), and returns an int status (0 = VLAK_OK). No torch types cross this
+ * boundary. Launches are asynchronous on the given stream; nothing here
+ * synchronizes the device. On a nonzero status, vlak_last_error_message()
+ * holds a one-line description (thread-local).
+ *
+ * Inputs are borrowed for the duration of the launch; outputs are written in
+ * place and owned by the caller. None of the entry points allocates device
+ * memory.
+ */
+#ifndef VLAK_B200_H_
+#define VLAK_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VLAK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VLAK_API __attribute__((visibility("default")))
+#else
+#define VLAK_API
+#endif
+
+/* status codes */
+enum {
+  VLAK_OK = 0,
+  VLAK_ERR_INVALID_ARGUMENT = 1, /* a shape / size / parameter contract is violated */
+  VLAK_ERR_ALIGNMENT = 2,        /* a base address or stride breaks 16-byte alignment */
+  VLAK_ERR_UNSUPPORTED_DTYPE = 3,
+  VLAK_ERR_CUDA = 4,             /* a CUDA runtime / driver call failed */
+  VLAK_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait ran out */
+  VLAK_ERR_UNSUPPORTED_DEVICE = 6 /* the current device is not sm_100 */
+};
+
+/* element types */
+enum { VLAK_F32 = 0, VLAK_F16 = 1, VLAK_BF16 = 2, VLAK_F64 = 3 };
+
+/* Library identity and diagnostics. */
+VLAK_API int vlak_abi_version(void);
+VLAK_API const char* vlak_status_string(int status);
+VLAK_API const char* vlak_last_error_message(void);
+
+/*
+ * Device error word. Kernels whose waits are bounded record a failed wait
+ * here instead of hanging; the word is per device and sticky until read.
+ * vlak_device_error_read() copies it to *code (0 = none) and clears it. It is
+ * a synchronous call on the current device (use it between steps, not inside
+ * a captured graph).
+ */
+VLAK_API int vlak_device_error_read(int* code);
+
+/* ------------------------------------------------------------------------
+ * Row softmax over the last dimension of a contiguous [rows, cols] tensor.
+ *
+ * Replaces softmax_lastdim (kernels/softmax/softmax_kernels.cu:255-297) behind
+ * the schema vlak::softmax(Tensor x, int version=4) -> Tensor
+ * (kernels/softmax/softmax_kernels.cu:303-305).
+ *   x, y     : device pointers, rows*cols elements each, row-major, no padding
+ *   dtype    : VLAK_F32 / VLAK_F16 / VLAK_BF16 / VLAK_F64 (math is fp32 in
+ *              all cases, as in the reference's AT_DISPATCH body)
+ *   version  : 0..4 selects the algorithm family (0 thread-per-row,
+ *              1 warp-per-row, 2 block-per-row 3-pass, 3 block-per-row
+ *              online 2-pass, 4 register-resident single read); any other
+ *              value behaves as 4, as in the reference dispatcher.
+ * rows == 0 or cols == 0 is a no-op. A row whose entries are all -inf
+ * produces NaN, as torch.softmax does.
+ * ---------------------------------------------------------------------- */
+VLAK_API int vlak_softmax_fwd(const void* x, void* y, int64_t rows, int64_t cols,
+                     int dtype, int version, void* stream);
+
+/* The version "auto" resolves to, restating _auto_version
+ * (kernels/softmax/__init__.py:26-37): cols > 2048 -> 4; rows >= 32 -> 1;
+ * else 4. */
+VLAK_API int vlak_softmax_auto_version(int64_t rows, int64_t cols);
+
+/* ------------------------------------------------------------------------
+ * GQA-native fused attention, head_dim 64, bf16 in / bf16 out, fp32 accumulate.
+ *
+ * Replaces the host functions fused_attention_gqa
+ * (kernels/attention/fused_attention.cu:603-669) and fused_attention_gqa_v4
+ * (kernels/attention/fused_attention_v4.cu:278-331) behind the schemas
+ * vlak::fused_attention_gqa / vlak::fused_attention_gqa_v4
+ * (fused_attention.cu:671-676, fused_attention_v4.cu:333-336).
+ *
+ * Logical shapes: q (B, M, H, 64), k and v (B, N, Hkv, 64), o (B, M, H, 64).
+ * Strides are in ELEMENTS for dims (0, 1, 2); dim 3 (head_dim) must be
+ * contiguous. Query head h reads kv head h / (H / Hkv).
+ *
+ * Mask (analytic, no tensor):
+ *   visible(r, c) = c < P ? (c < dead_start || c >= dead_end)
+ *                         : c <= (N - M) + r
+ * with P = prefix_len >= 0 ? prefix_len : N. scale <= 0 selects 1/sqrt(64).
+ * A query row with no visible key is written as exact zeros.
+ *
+ * Contract (checked before anything is launched; violations return
+ * VLAK_ERR_INVALID_ARGUMENT / VLAK_ERR_ALIGNMENT):
+ *   H % Hkv == 0, H / Hkv <= 128, 0 <= dead_start <= dead_end <= P <= N,
+ *   every pointer 16-byte aligned, every stride a multiple of 8 elements.
+ * B == 0 or M == 0 is a no-op; N == 0 writes zeros.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t B, M, N, H, Hkv;
+  int64_t q_stride[3]; /* (b, m, h) element strides of q */
+  int64_t k_stride[3]; /* (b, n, h_kv) element strides of k */
+  int64_t v_stride[3]; /* (b, n, h_kv) element strides of v */
+  int64_t o_stride[3]; /* (b, m, h) element strides of o */
+  double scale;
+  int64_t prefix_len;
+  int64_t dead_start;
+  int64_t dead_end;
+} vlak_attn_gqa_args;
+
+/* vlak::fused_attention_gqa (reference v3 contract). */
+VLAK_API int vlak_attn_gqa_fwd(const vlak_attn_gqa_args* args, void* stream);
+
+/* vlak::fused_attention_gqa_v4 (reference v4 contract). Same arguments and
+ * results as vlak_attn_gqa_fwd; both run the tcgen05 kernel. */
+VLAK_API int vlak_attn_gqa_v4_fwd(const vlak_attn_gqa_args* args, void* stream);
+
+/* Resolve the analytic-mask parameters exactly as the launch does
+ * (P = -1 -> N, scale <= 0 -> 1/8) and validate the contract without
+ * touching the device. Returns the status the launch would return for these
+ * arguments; writes the resolved values when the pointers are non-NULL. */
+VLAK_API int vlak_attn_gqa_check(const vlak_attn_gqa_args* args, int64_t* prefix_out,
+                        float* scale_out);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* VLAK_B200_H_ */

@@ -1,0 +1,160 @@
+"""GPU parity of vlak::softmax against the CPU oracle (and torch.softmax).
+
+Tolerances: fp32 max relative error <= 1e-6; fp16/bf16 atol 1e-2, rtol 1.6e-2
+against the fp32 oracle. Versions 0-4 all run the same
+checks, through the torch op and through the C ABI.
+"""
+import numpy as np
+import pytest
+import torch
+
+from kernels import workloads as wl
+from kernels.softmax import VERSIONS, softmax
+from oracle import softmax_rows
+from tests import capi
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1, 16), (8, 31), (128, 64), (1024, 128), (256, 1000), (4, 4096),
+          (33, 241), (7, 291), (5, 2049), (3, 8193), (2, 32768), (1, 40000), (64, 1)]
+DTYPES = [torch.float32, torch.float16, torch.bfloat16]
+
+
+def check(out, x, dtype):
+    ref = softmax_rows(x.float().cpu().numpy())
+    got = out.double().cpu().numpy()
+    if dtype in (torch.float32, torch.float64):
+        pos = ref > 0
+        rel = np.abs(got[pos] - ref[pos]) / ref[pos]
+        assert rel.max(initial=0) <= 1e-6, f"max rel err {rel.max()}"
+        assert np.array_equal(got[~pos], ref[~pos])
+    else:
+        torch.testing.assert_close(torch.from_numpy(got), torch.from_numpy(ref),
+                                   atol=1e-2, rtol=1.6e-2)
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", SHAPES)
+def test_matches_oracle(version, dtype, shape):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.randn(*shape, device="cuda", generator=g) * 3).to(dtype)
+    check(softmax(x, version=version), x, dtype)
+
+
+@pytest.mark.parametrize("version", [0, 1, 2, 3, 4, 7])
+def test_c1_full_size_fp32_with_neg_inf(version):
+    x = wl.softmax_c1()
+    assert torch.isinf(x).sum(1).eq(51).all()
+    out = softmax(x, version)
+    check(out, x, torch.float32)
+    assert (out[torch.isinf(x)] == 0).all()
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+def test_c1_matches_torch_softmax_fp32(version):
+    x = wl.softmax_c1()
+    ref = torch.softmax(x, -1)
+    out = softmax(x, version)
+    pos = ref > 0
+    rel = ((out[pos].double() - ref[pos].double()).abs() / ref[pos].double()).max().item()
+    assert rel <= 1e-6
+
+
+@pytest.mark.parametrize("rows", wl.C2_ROWS)
+@pytest.mark.parametrize("cols", wl.C2_COLS)
+def test_c2_sweep_bf16(rows, cols):
+    x = wl.softmax_c2(rows, cols)
+    out = softmax(x, "auto")
+    # full check on a subset of rows (oracle cost), row sums everywhere
+    idx = torch.arange(0, rows, max(1, rows // 64), device="cuda")
+    check(out[idx], x[idx], torch.bfloat16)
+    sums = out.float().sum(-1)
+    assert ((sums - 1).abs() < 2e-2 + cols * 4e-3 * 2 ** -8).all()
+
+
+def test_c2_narrow_many_rows_bf16():
+    rows, cols = wl.C2_NARROW
+    x = wl.softmax_c2(rows, cols, seed=3)
+    out = softmax(x, "auto")
+    idx = torch.randint(0, rows, (2048,), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    check(out[idx], x[idx], torch.bfloat16)
+    assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+def test_extreme_values_are_stable(version):
+    # tests/test_softmax.py:55-61
+    x = torch.tensor([[1000.0, 1001.0, 999.0, -1000.0]], device="cuda")
+    out = softmax(x, version=version)
+    assert torch.isfinite(out).all()
+    torch.testing.assert_close(out.sum(dim=-1), torch.ones(1, device="cuda"), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+def test_all_neg_inf_row_is_nan_like_torch(version):
+    x = torch.randn(3, 300, device="cuda")
+    x[1] = float("-inf")
+    out = softmax(x, version)
+    assert torch.isnan(out[1]).all() and torch.isfinite(out[[0, 2]]).all()
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_offset_view_input(version, dtype):
+    # x starts 1 element past a 16-byte boundary while y is aligned
+    base = torch.randn(37 * 291 + 1, device="cuda").to(dtype)
+    x = base[1:].view(37, 291)
+    check(softmax(x, version), x, dtype)
+
+
+def test_float64_input_computed_like_reference():
+    x = torch.randn(16, 777, device="cuda", dtype=torch.float64)
+    out = softmax(x, 4)
+    assert out.dtype == torch.float64
+    check(out.float(), x.float(), torch.float32)
+
+
+def test_empty_tensors():
+    for shape in [(0, 16), (16, 0)]:
+        x = torch.empty(*shape, device="cuda")
+        assert softmax(x, 4).shape == shape
+
+
+def test_non_contiguous_input_is_made_contiguous():
+    x = torch.randn(64, 300, device="cuda").t()
+    out = softmax(x, 1)
+    assert out.is_contiguous()
+    check(out, x.contiguous(), torch.float32)
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_through_c_abi(version, dtype):
+    x = (torch.randn(100, 1000, device="cuda") * 4).to(dtype)
+    st, y = capi.softmax(x, VERSIONS[version])
+    assert st == capi.VLAK_OK, capi.last_error()
+    torch.cuda.synchronize()
+    check(y, x, dtype)
+    assert torch.equal(y, softmax(x, version))
+
+
+def test_registered_op_and_compile():
+    # tests/test_softmax.py:64-90
+    x = torch.randn(16, 128, device="cuda")
+    torch.testing.assert_close(torch.ops.vlak.softmax(x, 1), torch.softmax(x, -1),
+                               rtol=1e-5, atol=1e-6)
+
+    def f(x):
+        return softmax(x, "v4") * 2.0
+
+    softmax(x, "v4")
+    out = torch.compile(f, fullgraph=True)(x)
+    torch.testing.assert_close(out, torch.softmax(x, -1) * 2.0, rtol=1e-4, atol=1e-5)
+
+
+def test_patch_kernels_style_call():
+    # vla/patch_kernels.py:26-36 reshapes N-d last-dim softmax to 2D and calls "auto"
+    x = torch.randn(2, 15, 50, 291, device="cuda")
+    out = softmax(x.reshape(-1, 291), "auto").reshape(x.shape)
+    torch.testing.assert_close(out, torch.softmax(x, -1), rtol=1e-5, atol=1e-6)

@@ -1,0 +1,689 @@
+// GQA-native fused attention for sm_100a: tcgen05 tensor cores with TMEM
+// accumulators, TMA-staged Q/K/V, analytic prefix / dead-band / staircase mask.
+//
+// Contract (the reference's v3/v4 host functions,
+// kernels/attention/fused_attention.cu:603-669 and fused_attention_v4.cu:278-331):
+//   q (B, M, H, 64), k/v (B, N, Hkv, 64) at arbitrary strides with head_dim
+//   innermost, bf16; o (B, M, H, 64) bf16; query head h reads kv head h / G;
+//   visible(r, c) = c < P ? (c < ds || c >= de) : c <= (N - M) + r
+//   (reference mask predicate: fused_attention.cu:378-398, :437-445).
+// Difference by design: a query row with no visible key is written as exact
+// zeros (the reference v3 produces NaN there, v4 leaves the row unwritten).
+//
+// Work decomposition. One work item = (b, kv head, block of query positions).
+// The G query heads of a kv head share K/V, so an item stacks its rows as
+// r = m_local * G + g (the order in which q stores them) into up to two
+// 128-row M-tiles; K/V are read once per item and reused by all G heads.
+// Items are distributed over a persistent grid of one CTA per SM.
+//
+// Roles inside a CTA (12 warps = 3 warpgroups):
+//   warps 0-3   softmax for M-tile 0, one TMEM lane (query row) per thread
+//   warps 4-7   softmax for M-tile 1
+//   warp 8      TMA producer: Q tiles (double-buffered across items) and
+//               128-key K/V chunks through a 4-stage ring.
+//   warp 9      TMEM allocator and MMA issuer (one thread):
+//               S_t = Q_t K_c^T  (SS MMA, M=128, N=chunk width, K=64)
+//               O_t (+)= P_t V_c (TS MMA: P from TMEM, V from smem, N=64)
+//   warps 10-11 idle
+// A softmax thread reads its row of S from TMEM twice (max, then exp), 32
+// keys at a time, so its register footprint stays small.
+// The two softmax groups ping-pong with the tensor core: while one group
+// turns S into P, the MMA warp runs the other tile's products.
+//
+// Tensor memory (512 columns x 128 lanes, fp32 cells):
+//   [0,128) S0  [128,256) S1  [256,320) P0  [320,384) P1  [384,448) O0  [448,512) O1
+// P holds bf16 pairs (two keys per 32-bit column), the A-operand layout of
+// the TS MMA.
+//
+// Online softmax in the exp2 domain with a lazily updated row max: the
+// reference max only moves (and O / l are rescaled in TMEM) when a new chunk's
+// max exceeds it by more than 8 (a factor 256), so P stays <= 256 in bf16 and
+// rescales are rare.
+//
+// Every mbarrier wait is bounded (1 s); on expiry the kernel records
+// VLAK_ERR_DEVICE_TIMEOUT in the device error word, drains its own TMA and
+// MMA work, frees TMEM and exits.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+
+#include "vlak_device.cuh"
+#include "vlak_internal.h"
+
+namespace vlak {
+
+// Device error word of this library (see vlak_device_error_read).
+__device__ int g_device_error = 0;
+
+namespace {
+
+__device__ __forceinline__ void record_device_error(int code) {
+  atomicCAS(&g_device_error, 0, code);
+}
+
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s per wait
+
+// Bounded parity wait; `abort_flag` (shared) short-circuits the other
+// waiters of the CTA once one of them has given up.
+__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
+                                             volatile int* abort_flag,
+                                             bool honour_abort = true) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 31u) == 0) {
+      if (honour_abort && *abort_flag) return false;
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > kWaitLimitNs) {
+        record_device_error(VLAK_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+constexpr int kThreads = 384;   // 3 warpgroups
+constexpr int kWarpProducer = 8, kWarpMma = 9;
+constexpr int kChunk = 128;   // keys per K/V chunk (S tile width)
+constexpr int kStages = 4;    // K/V ring depth
+constexpr int kRowBytes = 128;  // 64 bf16 per row
+constexpr int kTileBytes = 128 * kRowBytes;       // one 128-row operand tile
+constexpr int kQBytes = 2 * 2 * kTileBytes;        // 2 buffers x 2 M-tiles
+constexpr int kKVBytes = kStages * kTileBytes;     // K ring (V ring the same)
+constexpr int kSmemData = kQBytes + 2 * kKVBytes;  // 192 KB
+constexpr int kSmemBytes = kSmemData + 256 + 1024; // + barriers + alignment slack
+
+constexpr uint32_t kColS0 = 0, kColS1 = 128, kColP0 = 256, kColP1 = 320, kColO0 = 384,
+                   kColO1 = 448;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+struct __align__(64) Params {
+  CUtensorMap tm_q;  // dims (64, H, M, B), box (64, G, MT, 1)
+  CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 128, 1)
+  CUtensorMap tm_v;
+  __nv_bfloat16* o;
+  long long o_sb, o_sm, o_sh;  // element strides of o
+  int B, M, N, H, Hkv, G;
+  int MT;       // query positions per M-tile
+  int tiles;    // M-tiles per item (1 or 2)
+  int n_mblk;   // query-position blocks per (b, kv head)
+  int num_items;
+  int P, ds, de;
+  float scale_log2;  // softmax scale * log2(e)
+};
+
+struct Barriers {
+  uint64_t q_full[2], q_empty[2];
+  uint64_t kv_full[kStages], kv_empty[kStages];
+  uint64_t s_full[2], p_full[2], o_full[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Item {
+  int b, kvh, m0;  // m0: first query position of the item
+  int tiles_active;
+};
+
+__device__ __forceinline__ Item decode_item(const Params& p, int item) {
+  Item it;
+  const int mblk = item % p.n_mblk;
+  const int bk = item / p.n_mblk;
+  it.kvh = bk % p.Hkv;
+  it.b = bk / p.Hkv;
+  it.m0 = mblk * p.tiles * p.MT;
+  it.tiles_active = (p.tiles == 2 && it.m0 + p.MT < p.M) ? 2 : 1;
+  return it;
+}
+
+// Number of key chunks and whether chunk c has any visible key for some row
+// of the item (all roles evaluate this identically).
+__device__ __forceinline__ bool chunk_live(const Params& p, const Item& it, int c) {
+  const int c0 = c * kChunk;
+  const int width = min(kChunk, p.N - c0);
+  const int m_hi = min(p.M, it.m0 + it.tiles_active * p.MT) - 1;
+  const int e2_hi = max(p.P, min(p.N, p.N - p.M + m_hi + 1));
+  return (c0 < p.ds) || (c0 + width > p.de && c0 < e2_hi);
+}
+__device__ __forceinline__ int chunk_cols(const Params& p, int c) {
+  const int width = min(kChunk, p.N - c * kChunk);
+  return (width + 15) & ~15;  // MMA N must be a multiple of 16
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gqa_attention_sm100(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte-swizzled operand tiles
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* q_smem = smem;                      // [2 buf][2 tile][128 x 128 B]
+  uint8_t* k_smem = smem + kQBytes;            // [stage][128 x 128 B]
+  uint8_t* v_smem = k_smem + kKVBytes;
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kSmemData);
+  volatile int* abort_flag = &bars->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->q_full[i], 1);
+      mbar_init(&bars->q_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp
+      mbar_init(&bars->o_full[i], 1);
+    }
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&bars->kv_full[i], 1);
+      mbar_init(&bars->kv_empty[i], 1);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  // Q rows that no TMA box covers feed only discarded rows; clear them once so
+  // they hold finite values.
+  for (int i = threadIdx.x; i < kQBytes / 16; i += kThreads)
+    reinterpret_cast<uint4*>(q_smem)[i] = make_uint4(0, 0, 0, 0);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const int n_chunks = (p.N + kChunk - 1) / kChunk;
+
+  if (warp == kWarpProducer) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&p.tm_q);
+      prefetch_tmap(&p.tm_k);
+      prefetch_tmap(&p.tm_v);
+      uint32_t qi = 0, kv = 0;
+      uint32_t q_armed[2] = {0, 0}, kv_armed[kStages] = {0, 0, 0, 0};
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
+        const Item it = decode_item(p, item);
+        const int qs = qi & 1;
+        if (!bounded_wait(&bars->q_empty[qs], ((qi >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
+        mbar_arrive_expect_tx(&bars->q_full[qs], qbytes);
+        ++q_armed[qs];
+        for (int t = 0; t < it.tiles_active; ++t)
+          tma_load_4d(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
+                      it.kvh * p.G, it.m0 + t * p.MT, it.b);
+        for (int c = 0; c < n_chunks; ++c) {
+          if (!chunk_live(p, it, c)) continue;
+          const int s = kv % kStages;
+          if (!bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
+          ++kv_armed[s];
+          tma_load_4d(k_smem + s * kTileBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+          tma_load_4d(v_smem + s * kTileBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+          ++kv;
+        }
+      }
+      // never leave the CTA with copies in flight: wait for the last phase
+      // armed on every full barrier (bounded, independent of the abort flag)
+      for (int i = 0; i < 2; ++i)
+        if (q_armed[i]) bounded_wait(&bars->q_full[i], (q_armed[i] - 1) & 1, abort_flag, false);
+      for (int s = 0; s < kStages; ++s)
+        if (kv_armed[s]) bounded_wait(&bars->kv_full[s], (kv_armed[s] - 1) & 1, abort_flag, false);
+    }
+    __syncwarp();  // reconverge before the CTA-wide barrier
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t qi = 0, kv = 0, pph[2] = {0, 0};
+      const uint32_t colS[2] = {kColS0, kColS1}, colP[2] = {kColP0, kColP1},
+                     colO[2] = {kColO0, kColO1};
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
+        const Item it = decode_item(p, item);
+        const int qs = qi & 1;
+        if (!bounded_wait(&bars->q_full[qs], (qi >> 1) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t q_base = smem_u32(q_smem + qs * 2 * kTileBytes);
+        // j counts the live chunks of this item; chunk j sits in ring stage (kv + j) % kStages
+        auto issue_s = [&](int t, int c, int j) {
+          const int s = (kv + j) % kStages;
+          const uint32_t idesc = idesc_bf16_f32(128, chunk_cols(p, c), false);
+          const uint32_t a0 = q_base + t * kTileBytes;
+          const uint32_t b0 = smem_u32(k_smem + s * kTileBytes);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)  // head_dim 64 = 4 x K16, 32 B apart in a swizzled row
+            umma_ss(tmem + colS[t], sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0);
+          umma_commit(&bars->s_full[t]);
+        };
+        auto issue_pv = [&](int t, int c, int j) {
+          const int s = (kv + j) % kStages;
+          const int ncols = chunk_cols(p, c);
+          const uint32_t idesc = idesc_bf16_f32(128, 64, true);
+          const uint32_t b0 = smem_u32(v_smem + s * kTileBytes);
+          for (int k = 0; k < ncols / 16; ++k)  // 16 keys = 8 packed columns of P, 2 KB of V
+            umma_ts(tmem + colO[t], tmem + colP[t] + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc,
+                    (j > 0 || k > 0) ? 1u : 0u);
+        };
+        auto wait_kv = [&](int j) {
+          const uint32_t n = kv + j;
+          if (!bounded_wait(&bars->kv_full[n % kStages], (n / kStages) & 1, abort_flag)) return false;
+          tc_fence_after();
+          return true;
+        };
+        auto wait_p = [&](int t) {
+          if (!bounded_wait(&bars->p_full[t], pph[t], abort_flag)) return false;
+          pph[t] ^= 1;
+          tc_fence_after();
+          return true;
+        };
+        auto next_live = [&](int c) {
+          for (; c < n_chunks; ++c)
+            if (chunk_live(p, it, c)) return c;
+          return -1;
+        };
+
+        int cur = next_live(0);
+        int j = 0;
+        if (cur >= 0) {
+          if (!wait_kv(0)) { ok = false; break; }
+          for (int t = 0; t < it.tiles_active; ++t) issue_s(t, cur, 0);
+          while (cur >= 0) {
+            const int nxt = next_live(cur + 1);
+            if (!wait_p(0)) { ok = false; break; }
+            issue_pv(0, cur, j);
+            if (nxt >= 0) {
+              if (!wait_kv(j + 1)) { ok = false; break; }
+              issue_s(0, nxt, j + 1);
+            }
+            if (it.tiles_active == 2) {
+              if (!wait_p(1)) { ok = false; break; }
+              issue_pv(1, cur, j);
+            }
+            umma_commit(&bars->kv_empty[(kv + j) % kStages]);
+            if (nxt >= 0 && it.tiles_active == 2) issue_s(1, nxt, j + 1);
+            cur = nxt;
+            ++j;
+          }
+          if (!ok) break;
+        }
+        for (int t = 0; t < it.tiles_active; ++t) umma_commit(&bars->o_full[t]);
+        umma_commit(&bars->q_empty[qs]);
+        kv += j;
+      }
+      // every issued MMA must complete before TMEM is released
+      umma_commit(&bars->drain);
+      bounded_wait(&bars->drain, 0, abort_flag, false);
+    }
+    __syncwarp();  // reconverge before the CTA-wide barrier and the dealloc
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ softmax
+    const int t = warp >> 2;                // M-tile of this group
+    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;    // TMEM lane = row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_off + (t ? kColS1 : kColS0);
+    const uint32_t tP = tmem + lane_off + (t ? kColP1 : kColP0);
+    const uint32_t tO = tmem + lane_off + (t ? kColO1 : kColO0);
+    const int m_local = row / p.G;
+    const int g = row - m_local * p.G;
+    uint32_t sph = 0, oph = 0;
+    bool ok = true;
+
+    for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
+      const Item it = decode_item(p, item);
+      if (t >= it.tiles_active) continue;
+      const int m_first = it.m0 + t * p.MT;        // first query position of this tile
+      const int m = m_first + m_local;
+      const bool valid = (m_local < p.MT) && (m < p.M);
+      // a warp whose rows are all invalid skips the arithmetic
+      const int warp_first_m = m_first + (quarter * 32) / p.G;
+      const bool warp_active = ((quarter * 32) / p.G < p.MT) && (warp_first_m < p.M);
+      const int e2 = max(p.P, min(p.N, p.N - p.M + m + 1));
+      float m_run = -INFINITY, l_run = 0.f;
+      int j = 0;
+      for (int c = 0; c < n_chunks; ++c) {
+        if (!chunk_live(p, it, c)) continue;
+        // warp-uniform outcome: the TMEM accesses below are warp-collective
+        if (!__all_sync(kFullMask, bounded_wait(&bars->s_full[t], sph, abort_flag))) { ok = false; break; }
+        sph ^= 1;
+        tc_fence_after();
+        if (warp_active) {
+          const int c0 = c * kChunk;
+          const int ncols = chunk_cols(p, c);
+          // Per 32-key group, warp-uniform classes: every lane's row sees all
+          // 32 keys (no mask arithmetic) or none of them (no exp).
+          uint32_t full_bits = 0, none_bits = 0;
+#pragma unroll
+          for (int gq = 0; gq < kChunk / 32; ++gq) {
+            const int g0 = c0 + 32 * gq;
+            const bool full = (g0 + 32 <= p.ds) || (g0 >= p.de && g0 + 32 <= e2);
+            const bool none = (g0 >= p.ds) && (g0 + 32 <= p.de || g0 >= e2);
+            full_bits |= (__all_sync(kFullMask, full) ? 1u : 0u) << gq;
+            none_bits |= (__all_sync(kFullMask, none) ? 1u : 0u) << gq;
+          }
+          // pass 1: row max over visible keys
+          float mx = -INFINITY;
+#pragma unroll
+          for (int gq = 0; gq < kChunk / 32; ++gq) {
+            if (32 * gq >= ncols || ((none_bits >> gq) & 1u)) continue;
+            float v[32];
+            tmem_ld32(tS + 32 * gq, v);
+            tmem_wait_ld();
+            if ((full_bits >> gq) & 1u) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+            } else {
+              const int g0 = c0 + 32 * gq;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int cc = g0 + i;
+                const bool vis = (cc < p.ds) || (cc >= p.de && cc < e2);
+                mx = fmaxf(mx, vis ? v[i] : -INFINITY);
+              }
+            }
+          }
+          const float mz = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
+          if (j == 0) {
+            m_run = mz;
+          } else {
+            const bool need = mz > m_run + kRescaleThreshold;
+            if (__any_sync(kFullMask, need)) {
+              // rescale this row's O (and l) to the new reference max; the
+              // previous P.V has completed (it was issued before this chunk's S)
+              const float alpha = need ? ex2(m_run - mz) : 1.f;
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                float o[32];
+                tmem_ld32(tO + 32 * half, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                tmem_st32f(tO + 32 * half, o);
+              }
+              l_run *= alpha;
+              if (need) m_run = mz;
+            }
+          }
+          // pass 2: P = exp2(s * scale_log2 - mref) as bf16 pairs into TMEM
+          const float mref = (m_run == -INFINITY) ? 0.f : m_run;
+          const float nref = -mref;
+          float lsum = 0.f;
+#pragma unroll
+          for (int gq = 0; gq < kChunk / 32; ++gq) {
+            if (32 * gq >= ncols) continue;
+            uint32_t pk[16];
+            if ((none_bits >> gq) & 1u) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) pk[i] = 0u;
+            } else {
+              float v[32];
+              tmem_ld32(tS + 32 * gq, v);
+              tmem_wait_ld();
+              if (!((full_bits >> gq) & 1u)) {
+                const int g0 = c0 + 32 * gq;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const int cc = g0 + i;
+                  const bool vis = (cc < p.ds) || (cc >= p.de && cc < e2);
+                  v[i] = vis ? v[i] : -INFINITY;
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const float p0 = ex2(fmaf(v[i], p.scale_log2, nref));
+                const float p1 = ex2(fmaf(v[i + 1], p.scale_log2, nref));
+                lsum += p0 + p1;
+                pk[i / 2] = pack_bf16x2(p0, p1);
+              }
+            }
+            tmem_st16(tP + 16 * gq, pk);
+          }
+          l_run += lsum;
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[t]);
+        ++j;
+      }
+      if (!ok) break;
+      // epilogue: O / l -> bf16 rows of o
+      if (!__all_sync(kFullMask, bounded_wait(&bars->o_full[t], oph, abort_flag))) { ok = false; break; }
+      oph ^= 1;
+      tc_fence_after();
+      if (warp_active) {
+        float o[2][32];
+        if (j > 0) {
+          tmem_ld32(tO, o[0]);
+          tmem_ld32(tO + 32, o[1]);
+          tmem_wait_ld();
+        }
+        if (valid) {
+          const bool any = l_run > 0.f;
+          const float inv = any ? 1.f / l_run : 0.f;
+          __nv_bfloat16* orow = p.o + static_cast<long long>(it.b) * p.o_sb +
+                                static_cast<long long>(m) * p.o_sm +
+                                static_cast<long long>(it.kvh * p.G + g) * p.o_sh;
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float a = any ? o[v >> 2][(v & 3) * 8 + 2 * e] * inv : 0.f;
+              const float b = any ? o[v >> 2][(v & 3) * 8 + 2 * e + 1] * inv : 0.f;
+              w[e] = pack_bf16x2(a, b);
+            }
+            reinterpret_cast<uint4*>(orow)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Zero-fill of o for N == 0 (every row fully masked).
+__global__ void zero_rows(__nv_bfloat16* o, long long o_sb, long long o_sm, long long o_sh, int B,
+                          int M, int H) {
+  const long long rows = static_cast<long long>(B) * M * H;
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; r < rows;
+       r += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long h = r % H, bm = r / H, m = bm % M, b = bm / M;
+    uint4* row = reinterpret_cast<uint4*>(o + b * o_sb + m * o_sm + h * o_sh);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) row[v] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+int encode_map(CUtensorMap* map, const void* base, int64_t d1, int64_t d2, int64_t d3,
+               int64_t s1, int64_t s2, int64_t s3, uint32_t box1, uint32_t box2,
+               const char* name) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return set_error(VLAK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  // a size-1 dimension is never stepped over; give it a harmless stride
+  auto fix = [](int64_t size, int64_t stride_bytes, int64_t fallback) {
+    return size == 1 ? fallback : stride_bytes;
+  };
+  const int64_t b1 = fix(d1, s1 * 2, 128);
+  const int64_t b2 = fix(d2, s2 * 2, b1 * d1);
+  const int64_t b3 = fix(d3, s3 * 2, b2 * d2);
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2),
+                        static_cast<cuuint64_t>(d3)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(b1), static_cast<cuuint64_t>(b2),
+                           static_cast<cuuint64_t>(b3)};
+  cuuint32_t box[4] = {64, box1, box2, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_errorf(VLAK_ERR_INVALID_ARGUMENT,
+                      "fused_attention_gqa: cannot describe %s to TMA (CUresult %d); strides "
+                      "must be multiples of 8 elements and the layout addressable",
+                      name, static_cast<int>(r));
+  return VLAK_OK;
+}
+
+}  // namespace
+
+// Validation shared by the launch and vlak_attn_gqa_check. Mirrors the
+// TORCH_CHECKs of fused_attention.cu:608-633 (shape, GQA ratio, alignment,
+// prefix / dead-band order) with the same acceptance set.
+static int validate(const vlak_attn_gqa_args* a, int64_t* P_out, float* scale_out) {
+  if (!a) return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: null arguments");
+  if (a->B < 0 || a->M < 0 || a->N < 0 || a->H <= 0 || a->Hkv <= 0)
+    return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: sizes must be non-negative and heads positive");
+  if (a->H % a->Hkv != 0)
+    return set_error(VLAK_ERR_INVALID_ARGUMENT, "query heads must be a multiple of kv heads");
+  if (a->H / a->Hkv > 128)
+    return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: at most 128 query heads per kv head");
+  if (a->B > INT32_MAX || a->M > INT32_MAX || a->N > INT32_MAX || a->H > INT32_MAX)
+    return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: size exceeds 2^31-1");
+  const int64_t P = a->prefix_len >= 0 ? a->prefix_len : a->N;
+  if (P > a->N) return set_error(VLAK_ERR_INVALID_ARGUMENT, "prefix_len exceeds kv length");
+  if (!(0 <= a->dead_start && a->dead_start <= a->dead_end && a->dead_end <= P))
+    return set_error(VLAK_ERR_INVALID_ARGUMENT, "dead band must satisfy 0 <= ds <= de <= prefix_len");
+  const void* ptrs[4] = {a->q, a->k, a->v, a->o};
+  const int64_t* strides[4] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride};
+  for (int i = 0; i < 4; ++i) {
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0)
+      return set_error(VLAK_ERR_ALIGNMENT, "strides/base must keep 16B alignment for cp.async");
+    for (int d = 0; d < 3; ++d)
+      if (strides[i][d] % 8 != 0)
+        return set_error(VLAK_ERR_ALIGNMENT, "strides/base must keep 16B alignment for cp.async");
+  }
+  if (P_out) *P_out = P;
+  if (scale_out) *scale_out = a->scale > 0 ? static_cast<float>(a->scale) : 0.125f;
+  return VLAK_OK;
+}
+
+static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
+  using namespace vlak;
+  clear_error();
+  int64_t P = 0;
+  float scale = 0.f;
+  int st = validate(a, &P, &scale);
+  if (st != VLAK_OK) return st;
+  if (a->B == 0 || a->M == 0) return VLAK_OK;
+  if (!a->q || !a->k || !a->v || !a->o)
+    return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: null tensor pointer");
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  DeviceInfo dev;
+  st = current_device_info(&dev);
+  if (st != VLAK_OK) return st;
+  if (dev.cc_major != 10)
+    return set_errorf(VLAK_ERR_UNSUPPORTED_DEVICE,
+                      "fused_attention_gqa: needs an sm_100 device (found sm_%d%d)", dev.cc_major,
+                      dev.cc_minor);
+  auto* o = static_cast<__nv_bfloat16*>(a->o);
+  if (a->N == 0) {
+    const long long rows = a->B * a->M * a->H;
+    const int blocks = static_cast<int>(std::min<long long>((rows + 255) / 256, 4096));
+    zero_rows<<<blocks, 256, 0, cs>>>(o, a->o_stride[0], a->o_stride[1], a->o_stride[2],
+                                      static_cast<int>(a->B), static_cast<int>(a->M),
+                                      static_cast<int>(a->H));
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VLAK_OK : set_cuda_error("fused_attention_gqa zero fill", e);
+  }
+
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  const int G = static_cast<int>(a->H / a->Hkv);
+  const int M = static_cast<int>(a->M);
+  prm.B = static_cast<int>(a->B);
+  prm.M = M;
+  prm.N = static_cast<int>(a->N);
+  prm.H = static_cast<int>(a->H);
+  prm.Hkv = static_cast<int>(a->Hkv);
+  prm.G = G;
+  prm.MT = std::min(128 / G, M);
+  prm.tiles = M > prm.MT ? 2 : 1;
+  prm.n_mblk = (M + prm.tiles * prm.MT - 1) / (prm.tiles * prm.MT);
+  const long long items = static_cast<long long>(prm.B) * prm.Hkv * prm.n_mblk;
+  if (items > INT32_MAX) return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: too many work items");
+  prm.num_items = static_cast<int>(items);
+  prm.P = static_cast<int>(P);
+  prm.ds = static_cast<int>(a->dead_start);
+  prm.de = static_cast<int>(a->dead_end);
+  prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.o = o;
+  prm.o_sb = a->o_stride[0];
+  prm.o_sm = a->o_stride[1];
+  prm.o_sh = a->o_stride[2];
+
+  st = encode_map(&prm.tm_q, a->q, a->H, a->M, a->B, a->q_stride[2], a->q_stride[1],
+                  a->q_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "q");
+  if (st != VLAK_OK) return st;
+  st = encode_map(&prm.tm_k, a->k, a->Hkv, a->N, a->B, a->k_stride[2], a->k_stride[1],
+                  a->k_stride[0], 1, kChunk, "k");
+  if (st != VLAK_OK) return st;
+  st = encode_map(&prm.tm_v, a->v, a->Hkv, a->N, a->B, a->v_stride[2], a->v_stride[1],
+                  a->v_stride[0], 1, kChunk, "v");
+  if (st != VLAK_OK) return st;
+
+  // One-time per-device opt-in to the large dynamic shared-memory carve-out.
+  static std::atomic<int> ready[64];
+  if (dev.device >= 64) return set_error(VLAK_ERR_CUDA, "device ordinal out of range");
+  if (ready[dev.device].load() == 0) {
+    cudaError_t e;
+    e = cudaFuncSetAttribute(gqa_attention_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+    if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa smem opt-in", e);
+    ready[dev.device].store(1);
+  }
+  const int grid = static_cast<int>(std::min<long long>(items, dev.sm_count));
+  gqa_attention_sm100<<<grid, kThreads, kSmemBytes, cs>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa launch failed", e);
+  return VLAK_OK;
+}
+
+}  // namespace vlak
+
+extern "C" int vlak_attn_gqa_check(const vlak_attn_gqa_args* args, int64_t* prefix_out,
+                                   float* scale_out) {
+  vlak::clear_error();
+  return vlak::validate(args, prefix_out, scale_out);
+}
+
+extern "C" int vlak_attn_gqa_fwd(const vlak_attn_gqa_args* args, void* stream) {
+  return vlak::launch_gqa(args, stream);
+}
+
+extern "C" int vlak_attn_gqa_v4_fwd(const vlak_attn_gqa_args* args, void* stream) {
+  return vlak::launch_gqa(args, stream);
+}
+
+extern "C" int vlak_device_error_read(int* code) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, vlak::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return vlak::set_cuda_error("vlak_device_error_read", e);
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(vlak::g_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return vlak::set_cuda_error("vlak_device_error_read", e);
+  if (code) *code = v;
+  return VLAK_OK;
+}

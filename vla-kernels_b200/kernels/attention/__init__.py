@@ -1,0 +1,90 @@
+"""GQA-native fused attention on B200 (sm_100a) behind ``torch.ops.vlak``.
+
+Same API as the reference module (kernels/attention/__init__.py):
+``fused_attention_gqa`` and ``fused_attention_gqa_v4`` with their fake (meta)
+implementations and register guards, so ``vla/variants.py`` routes to them
+unchanged and each call traces as one node under ``torch.compile``.
+
+Both ops run one tcgen05 kernel (vla-kernels_b200/csrc/attention_gqa.cu):
+QK^T and PV on the 5th-generation tensor cores with accumulators in tensor
+memory, Q/K/V staged by TMA, the G query heads of a kv head sharing its K/V
+tiles, the online softmax in registers and the prefix / dead-band / causal
+mask computed from indices.
+"""
+from __future__ import annotations
+
+from functools import lru_cache
+
+import torch
+
+from .. import _native
+
+
+@lru_cache(maxsize=1)
+def _ext():
+    _native.load_ops()
+    # the op returns a CONTIGUOUS (B, M, H, 64) tensor; the fake must promise
+    # the same strides (kernels/attention/__init__.py:26-30)
+    torch.library.register_fake("vlak::fused_attention_gqa")(
+        lambda q, k, v, scale=-1.0, prefix_len=-1, dead_start=0, dead_end=0:
+            torch.empty(q.shape, dtype=q.dtype, device=q.device))
+    return torch.ops.vlak
+
+
+@lru_cache(maxsize=1)
+def _ext_v4():
+    _native.load_ops()
+    torch.library.register_fake("vlak::fused_attention_gqa_v4")(
+        lambda q, k, v, scale=-1.0, prefix_len=-1, dead_start=0, dead_end=0:
+            torch.empty(q.shape, dtype=q.dtype, device=q.device))
+    return torch.ops.vlak
+
+
+_registered = False
+_registered_v4 = False
+
+
+def _ensure_registered():
+    global _registered
+    if not _registered:
+        _ext()
+        _registered = True
+
+
+def _ensure_registered_v4():
+    global _registered_v4
+    if not _registered_v4:
+        _ext_v4()
+        _registered_v4 = True
+
+
+def fused_attention_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                        scale: float | None = None,
+                        prefix_len: int | None = None,
+                        dead_start: int = 0,
+                        dead_end: int = 0) -> torch.Tensor:
+    """GQA-native SDPA over the model's projection layouts.
+
+    q is (B, M, H, 64); k/v are (B, N, H_kv, 64) with H a multiple of H_kv,
+    consumed at their natural strides (no transpose/contiguous/expand). The
+    mask is arithmetic: visible(r, c) = c < prefix_len ? (c < dead_start or
+    c >= dead_end) : c <= (N - M) + r. Returns (B, M, H, 64) contiguous, so
+    .reshape(B, M, H*64) is a view. bf16 only. Rows with no visible key are
+    exact zeros.
+    """
+    _ensure_registered()
+    return torch.ops.vlak.fused_attention_gqa(
+        q, k, v, -1.0 if scale is None else scale,
+        -1 if prefix_len is None else prefix_len, dead_start, dead_end)
+
+
+def fused_attention_gqa_v4(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           scale: float | None = None,
+                           prefix_len: int | None = None,
+                           dead_start: int = 0,
+                           dead_end: int = 0) -> torch.Tensor:
+    """The reference's v4 entry point; same contract as fused_attention_gqa."""
+    _ensure_registered_v4()
+    return torch.ops.vlak.fused_attention_gqa_v4(
+        q, k, v, -1.0 if scale is None else scale,
+        -1 if prefix_len is None else prefix_len, dead_start, dead_end)
