@@ -1,0 +1,488 @@
+#!/usr/bin/env python3
+"""Benchmark of the vlak hot path on B200 (one JSON line on rank 0).
+
+Workload: one flow-matching chunk of SmolVLA
+action-expert self-attention -- 16 expert layers x 10 denoising steps = 160
+calls of vlak::fused_attention_gqa_v4 on q (B, 50, 15, 64), k/v (B, 291, 5, 64)
+bf16 with the analytic prefix/staircase mask (P = 241) -- over B = 2048 policy
+queries, batch-sharded over the N GPUs of one node (strong scaling: total work
+fixed), followed by one NCCL all-gather of the chunk's output. A step is one
+chunk; the 160 calls of a step are replayed from a CUDA graph, as the compiled
+model runs them.
+
+Metric: whole-job attention calls per second (one call = one B=2048 call,
+all shards); µs/call = 1e6 / value. Inputs: 16 per-layer input sets (one per
+expert layer), each larger than L2 at every N, rotated through the chunk, so
+every call reads cold K/V/Q from HBM.
+
+Extra keys: roofline of the attention kernel (HBM-bound at this shape) and its
+tensor-pipe fraction, e2e through the torch op with pinned host buffers, the
+CPU baseline (oracle port on host cores, rank 0, N=1), clocks sampled during the
+timed region, and a softmax line (config C2 wide rows, 1 GPU).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "vla-kernels_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from kernels import workloads as wl  # noqa: E402
+
+GLOBAL_B = 2048
+LAYERS, FLOW_STEPS = 16, 10
+CALLS_PER_STEP = LAYERS * FLOW_STEPS
+METRIC = "GQA attn calls/s (SmolVLA expert self-attn C5, B=2048, 160 calls/chunk; us/call = 1e6/value)"
+UNIT = "calls/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------- helpers
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu
+    summary (profiles/<name>), line `traffic_bytes_per_launch: <int>`."""
+    path = os.path.join(REPO, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def shard(B: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous batch shard of rank `rank`: [lo, hi)."""
+    base, rem = divmod(B, world)
+    lo = rank * base + min(rank, rem)
+    return lo, lo + base + (1 if rank < rem else 0)
+
+
+# ---------------------------------------------------------------- our arm
+
+def bench_ours(args, rank, world, local):
+    from kernels.attention import fused_attention_gqa_v4
+
+    lo, hi = shard(GLOBAL_B, rank, world)
+    B = hi - lo
+    shape = wl.expert_shape(B)
+    scale = 0.125
+    # 16 per-layer input sets (seeded by layer and shard offset)
+    sets = [wl.attn_inputs(shape, seed=1000 * layer + lo) for layer in range(LAYERS)]
+
+    def chunk():
+        out = None
+        for step in range(FLOW_STEPS):
+            for layer in range(LAYERS):
+                q, k, v = sets[layer]
+                out = fused_attention_gqa_v4(q, k, v, scale=scale, prefix_len=shape.P)
+        return out
+
+    # capture the chunk in a CUDA graph (warm the op on a side stream first)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chunk()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = chunk()
+    gathered = torch.empty((GLOBAL_B,) + tuple(static_out.shape[1:]), device="cuda",
+                           dtype=static_out.dtype) if world > 1 else None
+
+    def step():
+        graph.replay()
+        if world > 1:
+            # outputs gathered over NVLink; shards are equal when world | 2048
+            dist.all_gather_into_tensor(gathered, static_out)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    barrier(world)
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1), world)
+    ms_per_step = ms / args.steps
+    calls_per_s = CALLS_PER_STEP * args.steps / (ms / 1e3)
+
+    # kernel-only timing of the attention launches (no all-gather), for the roofline
+    k0 = torch.cuda.Event(enable_timing=True)
+    k1 = torch.cuda.Event(enable_timing=True)
+    reps = max(2, args.steps // 2)
+    barrier(world)
+    k0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    k1.record(stream)
+    torch.cuda.synchronize()
+    launch_s = k0.elapsed_time(k1) / 1e3 / (reps * CALLS_PER_STEP)
+    launch_s = max_over_ranks(launch_s, world)
+
+    peaks, peak_src = load_peaks()
+    bytes_per_launch = wl.attn_bytes(shape)
+    flops_per_launch = wl.attn_flops(shape)
+    achieved_gbs = bytes_per_launch / launch_s / 1e9
+    achieved_tflops = flops_per_launch / launch_s / 1e12
+    traffic = profile_traffic("gqa_attention_sm100_c5.txt")
+    if traffic is not None and world > 1:
+        traffic = int(traffic * B / GLOBAL_B)
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peaks["hbm_gbs"],
+        "unit": "GB/s", "frac": round(achieved_gbs / peaks["hbm_gbs"], 4),
+        "traffic": traffic, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
+        if peak_src == "measured" else "fallback 6.65 TB/s",
+        "kernel": "gqa_attention_sm100", "us_per_launch": round(launch_s * 1e6, 3),
+        "algorithmic_bytes_per_launch": bytes_per_launch,
+        "tensor_tflops": round(achieved_tflops, 1),
+        "tensor_frac": round(achieved_tflops / peaks["bf16_tflops"], 4),
+        "flops_per_launch": flops_per_launch,
+    }
+
+    # e2e: through the torch op with pinned host buffers, copies timed
+    e2e = bench_e2e(args, rank, world, shape, lo)
+
+    line = {
+        "metric": METRIC, "value": round(calls_per_s, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "us_per_call": round(1e6 / calls_per_s, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v of the SmolVLA expert shapes)",
+        "config": {"workload": "C5: expert self-attn q(B,50,15,64) k/v(B,291,5,64) P=241, "
+                               "B=2048 sharded over GPUs, 160 calls/step + NCCL all-gather",
+                   "global_batch": GLOBAL_B, "per_gpu_batch": B, "calls_per_step": CALLS_PER_STEP,
+                   "parallelism": f"batch-shard x{world}",
+                   "l2": "inputs > L2: 16 rotating per-layer input sets, >=144 MB each",
+                   "cuda_graph": True},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": CALLS_PER_STEP * args.steps * world,
+        "clocks": clk,
+    }
+    if world > 1:
+        dist.barrier()
+    del graph
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(target_s=args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_softmax:
+        line["softmax"] = bench_softmax()
+    return line
+
+
+def bench_e2e(args, rank, world, shape, lo):
+    from kernels.attention import fused_attention_gqa_v4
+
+    q, k, v = wl.attn_inputs(shape, seed=lo)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    del q, k, v
+    steps = max(3, args.steps // 2)
+
+    def one():
+        dq = hq.to("cuda", non_blocking=True)
+        dk = hk.to("cuda", non_blocking=True)
+        dv = hv.to("cuda", non_blocking=True)
+        o = fused_attention_gqa_v4(dq, dk, dv, scale=0.125, prefix_len=shape.P)
+        ho.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        one()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    h2d = (hq.numel() + hk.numel() + hv.numel()) * 2 * world
+    d2h = ho.numel() * 2 * world
+    return {"value": round(steps / (ms / 1e3), 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "note": "one call per step through torch.ops.vlak.fused_attention_gqa_v4 with "
+                    "pinned host q/k/v copied in and o copied out inside the timed region"}
+
+
+def bench_softmax():
+    """C2 wide-row bf16 softmax (8192 x 32768) and C1 fp32, 1 GPU, cold inputs."""
+    from kernels.softmax import softmax
+
+    peaks, _ = load_peaks()
+    res = {}
+    for name, x in (("C2_bf16_8192x32768", wl.softmax_c2(8192, 32768)),
+                    ("C1_fp32_4096x1024", wl.softmax_c1())):
+        xs = [x] + ([x.clone() for _ in range(3)] if x.numel() * x.element_size() < 2**28 else [])
+        flush = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
+        for _ in range(3):
+            softmax(xs[0], "auto")
+        times = []
+        for i in range(10):
+            flush.zero_()  # evict L2 (256 MB > 126 MB)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            softmax(xs[i % len(xs)], "auto")
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / 1e3)
+        t = statistics.median(times)
+        nbytes = wl.softmax_bytes(x.shape[0], x.shape[1], x.element_size())
+        gbs = nbytes / t / 1e9
+        res[name] = {"us": round(t * 1e6, 2), "GB/s": round(gbs, 1),
+                     "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "l2": "flushed"}
+        del xs, flush
+    return res
+
+
+def cpu_baseline_sample(target_s: float = 10.0) -> dict:
+    """The oracle port of the reference's CPU path (torch SDPA, fp32, all host
+    threads) on a bounded sample of C5: B=32 queries per call, as many calls as
+    fit in ~target_s; reported in full-B calls/s."""
+    from oracle import gqa_attention_torch_cpu
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample_b = 32
+    s = wl.expert_shape(sample_b)
+    q, k, v = wl.attn_inputs(s, device="cpu", seed=5)
+    gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < target_s or n < 2:
+        gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
+        n += 1
+    dt = time.perf_counter() - t0
+    calls_full = n * sample_b / GLOBAL_B
+    return {"value": round(calls_full / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} calls of B={sample_b} (of 2048) C5 expert self-attn, torch SDPA "
+                      f"fp32 on host, {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------- reference arm
+
+def bench_reference(args, rank, world):
+    """The reference's CPU path (torch SDPA with bool mask + repeat_interleave
+    GQA, fp32, all host threads) on the same C5 config, rank 0 only."""
+    if rank != 0:
+        return None
+    from oracle import gqa_attention_torch_cpu
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample_b = 64
+    s = wl.expert_shape(sample_b)
+    q, k, v = wl.attn_inputs(s, device="cpu", seed=5)
+    for _ in range(args.warmup):
+        gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
+    dt = time.perf_counter() - t0
+    value = args.steps * sample_b / GLOBAL_B / dt
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) q/k/v of the SmolVLA expert shapes)",
+        "config": {"workload": "C5: expert self-attn q(B,50,15,64) k/v(B,291,5,64) P=241, "
+                               "B=2048; each step one call on a B=64 sample",
+                   "global_batch": GLOBAL_B, "sample_batch": sample_b,
+                   "parallelism": "host CPU (reference path has no GPU code for sm_100)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"B={sample_b} of 2048 per step, torch SDPA fp32"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------- profiling mode
+
+def profile_case(args):
+    """A few eager launches of one kernel on a small case (for ncu captures):
+    attention at C3/C5 shapes with --batch queries, or softmax --rows x --cols
+    bf16. Inputs of both exceed L2 at the default sizes."""
+    torch.cuda.set_device(0)
+    if args.case == "attn":
+        from kernels.attention import fused_attention_gqa_v4
+
+        s = wl.expert_shape(args.batch)
+        sets = [wl.attn_inputs(s, seed=i) for i in range(2)]
+        for i in range(args.calls):
+            q, k, v = sets[i % 2]
+            fused_attention_gqa_v4(q, k, v, scale=0.125, prefix_len=s.P)
+    else:
+        from kernels.softmax import softmax
+
+        x = wl.softmax_c2(args.rows, args.cols)
+        for _ in range(args.calls):
+            softmax(x, "auto")
+    torch.cuda.synchronize()
+    print(f"profile case {args.case} done")
+
+
+# ---------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-softmax", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--case", choices=["attn", "softmax"], default=None,
+                    help="profiling mode: a few eager calls of one kernel, no JSON line")
+    ap.add_argument("--batch", type=int, default=512)
+    ap.add_argument("--rows", type=int, default=8192)
+    ap.add_argument("--cols", type=int, default=32768)
+    ap.add_argument("--calls", type=int, default=4)
+    args = ap.parse_args()
+
+    if args.case is not None:
+        profile_case(args)
+        return
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = bench_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        line = bench_ours(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

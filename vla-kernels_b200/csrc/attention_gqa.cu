@@ -588,7 +588,8 @@ static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
   int st = validate(a, &P, &scale);
   if (st != VLAK_OK) return st;
   if (a->B == 0 || a->M == 0) return VLAK_OK;
-  if (!a->q || !a->k || !a->v || !a->o)
+  // with no keys only o is touched; empty k / v may carry null pointers
+  if (!a->o || (a->N > 0 && (!a->q || !a->k || !a->v)))
     return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: null tensor pointer");
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
   DeviceInfo dev;

@@ -264,8 +264,11 @@ __global__ void softmax_thread_row(const T* __restrict__ x, T* __restrict__ y, i
   float m = -INFINITY;
   for (int c = 0; c < cols; ++c) m = fmaxf(m, E::to_f(xr[c]));
   if (m == -INFINITY) m = NAN;
-  float s = 0.f;
-  for (int c = 0; c < cols; ++c) s += exp_shift<T>(E::to_f(xr[c]), m);
+  // one thread sums the whole row serially: a double accumulator keeps the
+  // fp32 result within the same 1e-6 relative bound as the tree reductions
+  double acc = 0.0;
+  for (int c = 0; c < cols; ++c) acc += exp_shift<T>(E::to_f(xr[c]), m);
+  const float s = static_cast<float>(acc);
   const float inv = 1.f / s;
   for (int c = 0; c < cols; ++c) yr[c] = E::from_f(normalize<T>(exp_shift<T>(E::to_f(xr[c]), m), s, inv));
 }
