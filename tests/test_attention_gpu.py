@@ -47,6 +47,9 @@ EXTRA = [
     (1, 64, 1024, 12, 12, 1024, 0, 0),
     (1, 20, 40, 128, 1, 40, 0, 0),
     (4, 50, 291, 15, 5, 241, 0, 0),
+    (1, 8, 256, 1, 1, 256, 0, 0),
+    (3, 8, 300, 1, 1, 300, 0, 0),
+    (2, 16, 1000, 2, 1, 1000, 300, 700),
 ]
 
 
@@ -59,7 +62,16 @@ def oracle(q, k, v, P, ds, de, scale=None):
                                           v.float().cpu().numpy(), P, ds, de, scale))
 
 
+def device_error() -> int:
+    import ctypes
+    code = ctypes.c_int(-1)
+    assert capi.lib().vlak_device_error_read(ctypes.byref(code)) == capi.VLAK_OK
+    return code.value
+
+
 def check(out, ref, P=None):
+    torch.cuda.synchronize()
+    assert device_error() == 0, "a bounded device wait expired inside the kernel"
     got = out.float().cpu().double()
     zero_rows = (ref == 0).all(dim=-1)
     assert (got[zero_rows] == 0).all(), "rows with no visible key must be exact zeros"
@@ -250,6 +262,7 @@ def test_stress_randomized():
             out = fused_attention_gqa(q, k, v, prefix_len=241, dead_start=196, dead_end=240)
         del junk
         ref = oracle(q, k, v, 241, 196, 240)
+        assert device_error() == 0
         cos = torch.nn.functional.cosine_similarity(out.float().cpu().double().flatten(),
                                                     ref.flatten(), dim=0).item()
         if cos < 0.999:
@@ -285,9 +298,6 @@ def test_through_c_abi(v4):
 
 
 def test_device_error_word_stays_clear():
-    import ctypes
     run(fused_attention_gqa, *CASES[1])
     torch.cuda.synchronize()
-    code = ctypes.c_int(-1)
-    assert capi.lib().vlak_device_error_read(ctypes.byref(code)) == capi.VLAK_OK
-    assert code.value == 0
+    assert device_error() == 0

@@ -19,12 +19,12 @@
 // Roles inside a CTA (12 warps = 3 warpgroups):
 //   warps 0-3   softmax for M-tile 0, one TMEM lane (query row) per thread
 //   warps 4-7   softmax for M-tile 1
-//   warp 8      TMA producer: Q tiles (double-buffered across items) and
-//               128-key K/V chunks through a 4-stage ring.
-//   warp 9      TMEM allocator and MMA issuer (one thread):
+//   warps 8-9   idle
+//   warp 10     TMA producer: Q tiles (double-buffered across items) and
+//               64-key K/V chunks through an 8-stage ring.
+//   warp 11     TMEM allocator and MMA issuer (one thread):
 //               S_t = Q_t K_c^T  (SS MMA, M=128, N=chunk width, K=64)
 //               O_t (+)= P_t V_c (TS MMA: P from TMEM, V from smem, N=64)
-//   warps 10-11 idle
 // A softmax thread reads its row of S from TMEM twice (max, then exp), 32
 // keys at a time, so its register footprint stays small.
 // The two softmax groups ping-pong with the tensor core: while one group
@@ -94,24 +94,30 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
 }
 
 constexpr int kThreads = 384;   // 3 warpgroups
-constexpr int kWarpProducer = 8, kWarpMma = 9;
-constexpr int kChunk = 128;   // keys per K/V chunk (S tile width)
-constexpr int kStages = 4;    // K/V ring depth
+// control warps sit on SM sub-partitions 2 and 3: sub-partition 0 also hosts
+// the softmax warp of the second M-tile's first lane quarter
+constexpr int kWarpProducer = 10, kWarpMma = 11;
+constexpr int kPolyEvery = 4;  // one key pair in kPolyEvery takes exp2 on the FMA pipe
+constexpr int kChunk = 64;      // keys per K/V chunk (S tile width)
+constexpr int kStages = 8;      // K/V ring depth (chunks)
 constexpr int kRowBytes = 128;  // 64 bf16 per row
-constexpr int kTileBytes = 128 * kRowBytes;       // one 128-row operand tile
+constexpr int kTileBytes = 128 * kRowBytes;        // one 128-row Q tile
+constexpr int kChunkBytes = kChunk * kRowBytes;    // one 64-key K (or V) chunk
 constexpr int kQBytes = 2 * 2 * kTileBytes;        // 2 buffers x 2 M-tiles
-constexpr int kKVBytes = kStages * kTileBytes;     // K ring (V ring the same)
+constexpr int kKVBytes = kStages * kChunkBytes;    // K ring (V ring the same)
 constexpr int kSmemData = kQBytes + 2 * kKVBytes;  // 192 KB
-constexpr int kSmemBytes = kSmemData + 256 + 1024; // + barriers + alignment slack
+constexpr int kBarrierBytes = 512;
+constexpr int kSmemBytes = kSmemData + kBarrierBytes + 1024;  // + alignment slack
 
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColP0 = 256, kColP1 = 320, kColO0 = 384,
-                   kColO1 = 448;
+// Tensor memory, per M-tile t (base 256 t): S double buffer [0,64) [64,128),
+// P double buffer [128,160) [160,192) (bf16 pairs), O [192,256).
+constexpr uint32_t kTileCols = 256, kColS = 0, kColP = 128, kColO = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 struct __align__(64) Params {
   CUtensorMap tm_q;  // dims (64, H, M, B), box (64, G, MT, 1)
-  CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 128, 1)
+  CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 64, 1)
   CUtensorMap tm_v;
   __nv_bfloat16* o;
   long long o_sb, o_sm, o_sh;  // element strides of o
@@ -127,11 +133,16 @@ struct __align__(64) Params {
 struct Barriers {
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], p_full[2], o_full[2];
+  // S and P are double-buffered per tile; each buffer has its own pair of
+  // barriers, so no barrier ever runs two phases ahead of its waiter
+  uint64_t s_full[2][2], p_full[2][2];  // [tile][buffer]
+  uint64_t pv_done[2], o_full[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
+
+static_assert(sizeof(Barriers) <= kBarrierBytes, "barrier block overflows its region");
 
 struct Item {
   int b, kvh, m0;  // m0: first query position of the item
@@ -149,14 +160,19 @@ __device__ __forceinline__ Item decode_item(const Params& p, int item) {
   return it;
 }
 
-// Number of key chunks and whether chunk c has any visible key for some row
-// of the item (all roles evaluate this identically).
+// Whether key chunk c has a visible key for some row of the item (every role
+// evaluates this identically, so all agree on the item's live chunks).
 __device__ __forceinline__ bool chunk_live(const Params& p, const Item& it, int c) {
   const int c0 = c * kChunk;
   const int width = min(kChunk, p.N - c0);
   const int m_hi = min(p.M, it.m0 + it.tiles_active * p.MT) - 1;
   const int e2_hi = max(p.P, min(p.N, p.N - p.M + m_hi + 1));
   return (c0 < p.ds) || (c0 + width > p.de && c0 < e2_hi);
+}
+__device__ __forceinline__ int next_live(const Params& p, const Item& it, int c, int n_chunks) {
+  for (; c < n_chunks; ++c)
+    if (chunk_live(p, it, c)) return c;
+  return -1;
 }
 __device__ __forceinline__ int chunk_cols(const Params& p, int c) {
   const int width = min(kChunk, p.N - c * kChunk);
@@ -170,7 +186,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* q_smem = smem;                      // [2 buf][2 tile][128 x 128 B]
-  uint8_t* k_smem = smem + kQBytes;            // [stage][128 x 128 B]
+  uint8_t* k_smem = smem + kQBytes;            // [stage][64 x 128 B]
   uint8_t* v_smem = k_smem + kKVBytes;
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kSmemData);
   volatile int* abort_flag = &bars->abort_flag;
@@ -182,8 +198,11 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->q_full[i], 1);
       mbar_init(&bars->q_empty[i], 1);
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&bars->s_full[i][b], 1);
+        mbar_init(&bars->p_full[i][b], 4);  // one arrival per softmax warp
+      }
+      mbar_init(&bars->pv_done[i], 1);
       mbar_init(&bars->o_full[i], 1);
     }
     for (int i = 0; i < kStages; ++i) {
@@ -216,7 +235,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
       uint32_t qi = 0, kv = 0;
-      uint32_t q_armed[2] = {0, 0}, kv_armed[kStages] = {0, 0, 0, 0};
+      uint32_t q_armed[2] = {0, 0}, kv_armed[kStages] = {};
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
         const Item it = decode_item(p, item);
@@ -228,14 +247,13 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         for (int t = 0; t < it.tiles_active; ++t)
           tma_load_4d(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
                       it.kvh * p.G, it.m0 + t * p.MT, it.b);
-        for (int c = 0; c < n_chunks; ++c) {
-          if (!chunk_live(p, it, c)) continue;
+        for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks)) {
           const int s = kv % kStages;
           if (!bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
+          mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kChunkBytes);
           ++kv_armed[s];
-          tma_load_4d(k_smem + s * kTileBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
-          tma_load_4d(v_smem + s * kTileBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+          tma_load_4d(k_smem + s * kChunkBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+          tma_load_4d(v_smem + s * kChunkBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
           ++kv;
         }
       }
@@ -249,10 +267,12 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     __syncwarp();  // reconverge before the CTA-wide barrier
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
+    // Per item, chunk j of tile t:  S_t(j) -> buffer j%2 (issued two chunks
+    // ahead), then, once softmax has turned it into P_t(j) (buffer j%2),
+    // O_t (+)= P_t(j) V(j). Issue order per chunk: PV_t(j) then S_t(j+2), so
+    // the commit of S_t(j+2) also covers PV_t(j) (same thread, in order).
     if (lane == 0) {
-      uint32_t qi = 0, kv = 0, pph[2] = {0, 0};
-      const uint32_t colS[2] = {kColS0, kColS1}, colP[2] = {kColP0, kColP1},
-                     colO[2] = {kColO0, kColO1};
+      uint32_t qi = 0, kv = 0, pph[2][2] = {{0, 0}, {0, 0}};
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
         const Item it = decode_item(p, item);
@@ -260,25 +280,27 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         if (!bounded_wait(&bars->q_full[qs], (qi >> 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t q_base = smem_u32(q_smem + qs * 2 * kTileBytes);
-        // j counts the live chunks of this item; chunk j sits in ring stage (kv + j) % kStages
         auto issue_s = [&](int t, int c, int j) {
           const int s = (kv + j) % kStages;
           const uint32_t idesc = idesc_bf16_f32(128, chunk_cols(p, c), false);
           const uint32_t a0 = q_base + t * kTileBytes;
-          const uint32_t b0 = smem_u32(k_smem + s * kTileBytes);
+          const uint32_t b0 = smem_u32(k_smem + s * kChunkBytes);
+          const uint32_t d = tmem + t * kTileCols + kColS + (j & 1) * kChunk;
 #pragma unroll
           for (int k = 0; k < 4; ++k)  // head_dim 64 = 4 x K16, 32 B apart in a swizzled row
-            umma_ss(tmem + colS[t], sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0);
-          umma_commit(&bars->s_full[t]);
+            umma_ss(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0);
+          umma_commit(&bars->s_full[t][j & 1]);
         };
         auto issue_pv = [&](int t, int c, int j) {
           const int s = (kv + j) % kStages;
           const int ncols = chunk_cols(p, c);
           const uint32_t idesc = idesc_bf16_f32(128, 64, true);
-          const uint32_t b0 = smem_u32(v_smem + s * kTileBytes);
+          const uint32_t b0 = smem_u32(v_smem + s * kChunkBytes);
+          const uint32_t a = tmem + t * kTileCols + kColP + (j & 1) * (kChunk / 2);
+          const uint32_t d = tmem + t * kTileCols + kColO;
           for (int k = 0; k < ncols / 16; ++k)  // 16 keys = 8 packed columns of P, 2 KB of V
-            umma_ts(tmem + colO[t], tmem + colP[t] + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc,
-                    (j > 0 || k > 0) ? 1u : 0u);
+            umma_ts(d, a + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&bars->pv_done[t]);
         };
         auto wait_kv = [&](int j) {
           const uint32_t n = kv + j;
@@ -286,42 +308,39 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           tc_fence_after();
           return true;
         };
-        auto wait_p = [&](int t) {
-          if (!bounded_wait(&bars->p_full[t], pph[t], abort_flag)) return false;
-          pph[t] ^= 1;
+        auto wait_p = [&](int t, int j) {
+          if (!bounded_wait(&bars->p_full[t][j & 1], pph[t][j & 1], abort_flag)) return false;
+          pph[t][j & 1] ^= 1;
           tc_fence_after();
           return true;
         };
-        auto next_live = [&](int c) {
-          for (; c < n_chunks; ++c)
-            if (chunk_live(p, it, c)) return c;
-          return -1;
-        };
 
-        int cur = next_live(0);
+        int cur = next_live(p, it, 0, n_chunks);
+        int nxt = cur >= 0 ? next_live(p, it, cur + 1, n_chunks) : -1;
         int j = 0;
         if (cur >= 0) {
           if (!wait_kv(0)) { ok = false; break; }
           for (int t = 0; t < it.tiles_active; ++t) issue_s(t, cur, 0);
-          while (cur >= 0) {
-            const int nxt = next_live(cur + 1);
-            if (!wait_p(0)) { ok = false; break; }
-            issue_pv(0, cur, j);
-            if (nxt >= 0) {
-              if (!wait_kv(j + 1)) { ok = false; break; }
-              issue_s(0, nxt, j + 1);
-            }
-            if (it.tiles_active == 2) {
-              if (!wait_p(1)) { ok = false; break; }
-              issue_pv(1, cur, j);
-            }
-            umma_commit(&bars->kv_empty[(kv + j) % kStages]);
-            if (nxt >= 0 && it.tiles_active == 2) issue_s(1, nxt, j + 1);
-            cur = nxt;
-            ++j;
+        }
+        if (nxt >= 0) {
+          if (!wait_kv(1)) { ok = false; break; }
+          for (int t = 0; t < it.tiles_active; ++t) issue_s(t, nxt, 1);
+        }
+        while (cur >= 0) {
+          const int nn = nxt >= 0 ? next_live(p, it, nxt + 1, n_chunks) : -1;  // chunk j+2
+          if (nn >= 0 && !wait_kv(j + 2)) { ok = false; break; }
+          for (int t = 0; t < it.tiles_active; ++t) {
+            if (!wait_p(t, j)) { ok = false; break; }
+            issue_pv(t, cur, j);
+            if (nn >= 0) issue_s(t, nn, j + 2);
           }
           if (!ok) break;
+          umma_commit(&bars->kv_empty[(kv + j) % kStages]);
+          cur = nxt;
+          nxt = nn;
+          ++j;
         }
+        if (!ok) break;
         for (int t = 0; t < it.tiles_active; ++t) umma_commit(&bars->o_full[t]);
         umma_commit(&bars->q_empty[qs]);
         kv += j;
@@ -336,13 +355,11 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     const int t = warp >> 2;                // M-tile of this group
     const int quarter = warp & 3;           // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;    // TMEM lane = row within the tile
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (t ? kColS1 : kColS0);
-    const uint32_t tP = tmem + lane_off + (t ? kColP1 : kColP0);
-    const uint32_t tO = tmem + lane_off + (t ? kColO1 : kColO0);
+    const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + t * kTileCols;
+    const uint32_t tO = tbase + kColO;
     const int m_local = row / p.G;
     const int g = row - m_local * p.G;
-    uint32_t sph = 0, oph = 0;
+    uint32_t sph[2] = {0, 0}, oph = 0, pv_seen = 0;  // pv_seen: P.V products of this tile so far
     bool ok = true;
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
@@ -357,73 +374,80 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       const int e2 = max(p.P, min(p.N, p.N - p.M + m + 1));
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
-      for (int c = 0; c < n_chunks; ++c) {
-        if (!chunk_live(p, it, c)) continue;
+      for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks), ++j) {
         // warp-uniform outcome: the TMEM accesses below are warp-collective
-        if (!__all_sync(kFullMask, bounded_wait(&bars->s_full[t], sph, abort_flag))) { ok = false; break; }
-        sph ^= 1;
+        if (!__all_sync(kFullMask, bounded_wait(&bars->s_full[t][j & 1], sph[j & 1], abort_flag))) {
+          ok = false;
+          break;
+        }
+        sph[j & 1] ^= 1;
         tc_fence_after();
         if (warp_active) {
           const int c0 = c * kChunk;
           const int ncols = chunk_cols(p, c);
-          // Per 32-key group, warp-uniform classes: every lane's row sees all
-          // 32 keys (no mask arithmetic) or none of them (no exp).
+          const uint32_t tS = tbase + kColS + (j & 1) * kChunk;
+          const uint32_t tP = tbase + kColP + (j & 1) * (kChunk / 2);
+          // S of this chunk in one batch and one wait; columns past the chunk
+          // width fail the visibility test (they lie at or past N >= e2). The
+          // mask is applied where a value is used; S is never rewritten.
+          float sv[kChunk / 32][32];
+#pragma unroll
+          for (int gq = 0; gq < kChunk / 32; ++gq) tmem_ld32(tS + 32 * gq, sv[gq]);
+          // This row's visible keys within each 32-key group, as a bit mask
+          // (visible set [0, ds) U [de, e2)), and the warp-uniform classes
+          // "every row sees all 32 keys" / "no row sees any".
+          uint32_t vmask[kChunk / 32];
           uint32_t full_bits = 0, none_bits = 0;
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             const int g0 = c0 + 32 * gq;
-            const bool full = (g0 + 32 <= p.ds) || (g0 >= p.de && g0 + 32 <= e2);
-            const bool none = (g0 >= p.ds) && (g0 + 32 <= p.de || g0 >= e2);
-            full_bits |= (__all_sync(kFullMask, full) ? 1u : 0u) << gq;
-            none_bits |= (__all_sync(kFullMask, none) ? 1u : 0u) << gq;
+            auto low = [](int n) -> uint32_t {
+              return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+            };
+            uint32_t vm = low(p.ds - g0) | (low(e2 - g0) & ~low(p.de - g0));
+            if (32 * gq >= ncols) vm = 0u;
+            vmask[gq] = vm;
+            full_bits |= (__all_sync(kFullMask, vm == 0xffffffffu) ? 1u : 0u) << gq;
+            none_bits |= (__all_sync(kFullMask, vm == 0u) ? 1u : 0u) << gq;
           }
-          // pass 1: row max over visible keys
+          tmem_wait_ld();
           float mx = -INFINITY;
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
-            if (32 * gq >= ncols || ((none_bits >> gq) & 1u)) continue;
-            float v[32];
-            tmem_ld32(tS + 32 * gq, v);
-            tmem_wait_ld();
+            if ((none_bits >> gq) & 1u) continue;
             if ((full_bits >> gq) & 1u) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+              for (int i = 0; i < 32; i += 2) mx = fmax3(mx, sv[gq][i], sv[gq][i + 1]);
             } else {
-              const int g0 = c0 + 32 * gq;
+              const uint32_t vm = vmask[gq];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int cc = g0 + i;
-                const bool vis = (cc < p.ds) || (cc >= p.de && cc < e2);
-                mx = fmaxf(mx, vis ? v[i] : -INFINITY);
-              }
+              for (int i = 0; i < 32; i += 2)
+                mx = fmax3(mx, ((vm >> i) & 1u) ? sv[gq][i] : -INFINITY,
+                           ((vm >> (i + 1)) & 1u) ? sv[gq][i + 1] : -INFINITY);
             }
           }
           const float mz = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
+          // The reference max moves only when this chunk's max exceeds it by
+          // more than the threshold; O and l are then rescaled by alpha (after
+          // P is written, so S is no longer live).
+          bool need = false;
+          float alpha = 1.f;
           if (j == 0) {
             m_run = mz;
           } else {
-            const bool need = mz > m_run + kRescaleThreshold;
-            if (__any_sync(kFullMask, need)) {
-              // rescale this row's O (and l) to the new reference max; the
-              // previous P.V has completed (it was issued before this chunk's S)
-              const float alpha = need ? ex2(m_run - mz) : 1.f;
-#pragma unroll
-              for (int half = 0; half < 2; ++half) {
-                float o[32];
-                tmem_ld32(tO + 32 * half, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                tmem_st32f(tO + 32 * half, o);
-              }
-              l_run *= alpha;
-              if (need) m_run = mz;
+            need = mz > m_run + kRescaleThreshold;
+            if (need) {
+              alpha = ex2(m_run - mz);
+              m_run = mz;
             }
           }
-          // pass 2: P = exp2(s * scale_log2 - mref) as bf16 pairs into TMEM
-          const float mref = (m_run == -INFINITY) ? 0.f : m_run;
-          const float nref = -mref;
-          float lsum = 0.f;
+          // P = exp2(s * scale_log2 - mref) as bf16 pairs into TMEM. Key pairs
+          // go through the f32x2 FMA pipe; most exps run on MUFU, one pair in
+          // kPolyEvery on the FMA pipe (full groups only, where no -inf occurs).
+          const float nref = (m_run == -INFINITY) ? 0.f : -m_run;
+          const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2);
+          const uint64_t nr2 = f2_pack(nref, nref);
+          uint64_t acc = f2_pack(0.f, 0.f);
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             if (32 * gq >= ncols) continue;
@@ -431,36 +455,66 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
             if ((none_bits >> gq) & 1u) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) pk[i] = 0u;
-            } else {
-              float v[32];
-              tmem_ld32(tS + 32 * gq, v);
-              tmem_wait_ld();
-              if (!((full_bits >> gq) & 1u)) {
-                const int g0 = c0 + 32 * gq;
+            } else if ((full_bits >> gq) & 1u) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  const int cc = g0 + i;
-                  const bool vis = (cc < p.ds) || (cc >= p.de && cc < e2);
-                  v[i] = vis ? v[i] : -INFINITY;
+              for (int k = 0; k < 16; ++k) {
+                const uint64_t x = f2_fma(f2_pack(sv[gq][2 * k], sv[gq][2 * k + 1]), sl2, nr2);
+                uint64_t e;
+                float x0, x1;
+                f2_unpack(x, x0, x1);
+                if (k % kPolyEvery == kPolyEvery - 1) {
+                  e = f2_exp2_poly(f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f)));
+                } else {
+                  e = f2_pack(ex2(x0), ex2(x1));
                 }
+                acc = f2_add(acc, e);
+                float e0, e1;
+                f2_unpack(e, e0, e1);
+                pk[k] = pack_bf16x2(e0, e1);
               }
+            } else {
+              const uint32_t vm = vmask[gq];
 #pragma unroll
-              for (int i = 0; i < 32; i += 2) {
-                const float p0 = ex2(fmaf(v[i], p.scale_log2, nref));
-                const float p1 = ex2(fmaf(v[i + 1], p.scale_log2, nref));
-                lsum += p0 + p1;
-                pk[i / 2] = pack_bf16x2(p0, p1);
+              for (int k = 0; k < 16; ++k) {
+                const uint64_t x = f2_fma(f2_pack(sv[gq][2 * k], sv[gq][2 * k + 1]), sl2, nr2);
+                float x0, x1;
+                f2_unpack(x, x0, x1);
+                const float e0 = ((vm >> (2 * k)) & 1u) ? ex2(x0) : 0.f;
+                const float e1 = ((vm >> (2 * k + 1)) & 1u) ? ex2(x1) : 0.f;
+                acc = f2_add(acc, f2_pack(e0, e1));
+                pk[k] = pack_bf16x2(e0, e1);
               }
             }
             tmem_st16(tP + 16 * gq, pk);
           }
-          l_run += lsum;
+          float acc0, acc1;
+          f2_unpack(acc, acc0, acc1);
+          const float lsum = acc0 + acc1;
+          l_run = l_run * alpha + lsum;
           tmem_wait_st();
+          if (__any_sync(kFullMask, need)) {
+            // O_t must hold the previous P.V of this tile before it is scaled
+            if (!__all_sync(kFullMask, bounded_wait(&bars->pv_done[t], (pv_seen - 1) & 1, abort_flag))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              float o[32];
+              tmem_ld32(tO + 32 * half, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= alpha;
+              tmem_st32f(tO + 32 * half, o);
+            }
+            tmem_wait_st();
+          }
         }
+        ++pv_seen;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_full[t]);
-        ++j;
+        if (lane == 0) mbar_arrive(&bars->p_full[t][j & 1]);
       }
       if (!ok) break;
       // epilogue: O / l -> bf16 rows of o

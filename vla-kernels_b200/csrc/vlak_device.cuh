@@ -122,6 +122,55 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // ---------------------------------------------------------------------------
+// packed fp32 pairs (sm_100 f32x2 FMA-pipe instructions) and 3-input max
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x in [-126, 126] on the FMA pipe, leaving the MUFU unit
+// free. x = j + f with j = round(x), obtained by adding 1.5 * 2^23 (which
+// leaves j in the low mantissa bits), and f in [-1/2, 1/2]; 2^f is the cubic
+// interpolating it at the four Chebyshev nodes of [-1/2, 1/2] (relative error
+// below 1.1e-4, fitted for this file); 2^j is added into the exponent field.
+// Callers clamp x below at -126 so the exponent field never underflows.
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+  const uint64_t t = f2_add(x, f2_pack(kShift, kShift));
+  const uint64_t jf = f2_add(t, f2_pack(-kShift, -kShift));
+  const uint64_t f = f2_fma(jf, f2_pack(-1.f, -1.f), x);
+  uint64_t q = f2_fma(f2_pack(0.05583828315f, 0.05583828315f), f,
+                      f2_pack(0.24263948202f, 0.24263948202f));
+  q = f2_fma(q, f, f2_pack(0.69313675165f, 0.69313675165f));
+  q = f2_fma(q, f, f2_pack(0.99992454052f, 0.99992454052f));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  const uint32_t r0 = __float_as_uint(q0) + (__float_as_uint(t0) << 23);
+  const uint32_t r1 = __float_as_uint(q1) + (__float_as_uint(t1) << 23);
+  return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
+}
+
+// ---------------------------------------------------------------------------
 // shared-memory addresses, mbarriers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
