@@ -75,20 +75,20 @@ constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s per wait
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
                                              volatile int* abort_flag,
                                              bool honour_abort = true) {
-  if (mbar_try_wait(bar, parity)) return true;
+  // each try suspends the thread in hardware for up to 20 us while the phase
+  // is incomplete; the elapsed time is checked between tries
+  if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 31u) == 0) {
-      if (honour_abort && *abort_flag) return false;
-      uint64_t t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (t - t0 > kWaitLimitNs) {
-        record_device_error(VLAK_ERR_DEVICE_TIMEOUT);
-        *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+    if (honour_abort && *abort_flag) return false;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > kWaitLimitNs) {
+      record_device_error(VLAK_ERR_DEVICE_TIMEOUT);
+      *abort_flag = 1;
+      return false;
     }
   }
 }
@@ -97,7 +97,12 @@ constexpr int kThreads = 384;   // 3 warpgroups
 // control warps sit on SM sub-partitions 2 and 3: sub-partition 0 also hosts
 // the softmax warp of the second M-tile's first lane quarter
 constexpr int kWarpProducer = 10, kWarpMma = 11;
-constexpr int kPolyEvery = 4;  // one key pair in kPolyEvery takes exp2 on the FMA pipe
+// Key pairs whose exp2 runs on the FMA pipe instead of MUFU: bit (k % 8) of
+// the mask selects pair k of a 32-key group (full groups only).
+#ifndef VLAK_POLY_MASK
+#define VLAK_POLY_MASK 0x88u
+#endif
+constexpr uint32_t kPolyMask = VLAK_POLY_MASK;
 constexpr int kChunk = 64;      // keys per K/V chunk (S tile width)
 constexpr int kStages = 8;      // K/V ring depth (chunks)
 constexpr int kRowBytes = 128;  // 64 bf16 per row
@@ -105,7 +110,8 @@ constexpr int kTileBytes = 128 * kRowBytes;        // one 128-row Q tile
 constexpr int kChunkBytes = kChunk * kRowBytes;    // one 64-key K (or V) chunk
 constexpr int kQBytes = 2 * 2 * kTileBytes;        // 2 buffers x 2 M-tiles
 constexpr int kKVBytes = kStages * kChunkBytes;    // K ring (V ring the same)
-constexpr int kSmemData = kQBytes + 2 * kKVBytes;  // 192 KB
+constexpr int kOBytes = 2 * kTileBytes;            // output staging, one tile per M-tile
+constexpr int kSmemData = kQBytes + 2 * kKVBytes + kOBytes;  // 224 KB
 constexpr int kBarrierBytes = 512;
 constexpr int kSmemBytes = kSmemData + kBarrierBytes + 1024;  // + alignment slack
 
@@ -119,6 +125,7 @@ struct __align__(64) Params {
   CUtensorMap tm_q;  // dims (64, H, M, B), box (64, G, MT, 1)
   CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 64, 1)
   CUtensorMap tm_v;
+  CUtensorMap tm_o;  // dims (64, H, M, B) of o, box (64, G, MT, 1): tile stores
   __nv_bfloat16* o;
   long long o_sb, o_sm, o_sh;  // element strides of o
   int B, M, N, H, Hkv, G;
@@ -188,6 +195,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   uint8_t* q_smem = smem;                      // [2 buf][2 tile][128 x 128 B]
   uint8_t* k_smem = smem + kQBytes;            // [stage][64 x 128 B]
   uint8_t* v_smem = k_smem + kKVBytes;
+  uint8_t* o_smem = v_smem + kKVBytes;         // [tile][128 x 128 B], 128B-swizzled
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kSmemData);
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -234,8 +242,11 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
+      prefetch_tmap(&p.tm_o);
       uint32_t qi = 0, kv = 0;
-      uint32_t q_armed[2] = {0, 0}, kv_armed[kStages] = {};
+      // per full barrier: bit i of *_used = armed at least once, bit i of
+      // *_par = parity of its most recently armed phase (registers, no arrays)
+      uint32_t q_used = 0, q_par = 0, kv_used = 0, kv_par = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
         const Item it = decode_item(p, item);
@@ -243,7 +254,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         if (!bounded_wait(&bars->q_empty[qs], ((qi >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
         const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
         mbar_arrive_expect_tx(&bars->q_full[qs], qbytes);
-        ++q_armed[qs];
+        q_par = (q_used & (1u << qs)) ? (q_par ^ (1u << qs)) : q_par;
+        q_used |= 1u << qs;
         for (int t = 0; t < it.tiles_active; ++t)
           tma_load_4d(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
                       it.kvh * p.G, it.m0 + t * p.MT, it.b);
@@ -251,7 +263,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           const int s = kv % kStages;
           if (!bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kChunkBytes);
-          ++kv_armed[s];
+          kv_par = (kv_used & (1u << s)) ? (kv_par ^ (1u << s)) : kv_par;
+          kv_used |= 1u << s;
           tma_load_4d(k_smem + s * kChunkBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
           tma_load_4d(v_smem + s * kChunkBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
           ++kv;
@@ -260,9 +273,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       // never leave the CTA with copies in flight: wait for the last phase
       // armed on every full barrier (bounded, independent of the abort flag)
       for (int i = 0; i < 2; ++i)
-        if (q_armed[i]) bounded_wait(&bars->q_full[i], (q_armed[i] - 1) & 1, abort_flag, false);
+        if (q_used & (1u << i)) bounded_wait(&bars->q_full[i], (q_par >> i) & 1u, abort_flag, false);
       for (int s = 0; s < kStages; ++s)
-        if (kv_armed[s]) bounded_wait(&bars->kv_full[s], (kv_armed[s] - 1) & 1, abort_flag, false);
+        if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
     }
     __syncwarp();  // reconverge before the CTA-wide barrier
   } else if (warp == kWarpMma) {
@@ -272,7 +285,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     // O_t (+)= P_t(j) V(j). Issue order per chunk: PV_t(j) then S_t(j+2), so
     // the commit of S_t(j+2) also covers PV_t(j) (same thread, in order).
     if (lane == 0) {
-      uint32_t qi = 0, kv = 0, pph[2][2] = {{0, 0}, {0, 0}};
+      uint32_t qi = 0, kv = 0, pph = 0;  // bit 2t+b: parity expected on p_full[t][b]
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
         const Item it = decode_item(p, item);
@@ -309,8 +322,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           return true;
         };
         auto wait_p = [&](int t, int j) {
-          if (!bounded_wait(&bars->p_full[t][j & 1], pph[t][j & 1], abort_flag)) return false;
-          pph[t][j & 1] ^= 1;
+          const uint32_t bit = 1u << (2 * t + (j & 1));
+          if (!bounded_wait(&bars->p_full[t][j & 1], (pph & bit) ? 1u : 0u, abort_flag)) return false;
+          pph ^= bit;
           tc_fence_after();
           return true;
         };
@@ -359,7 +373,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     const uint32_t tO = tbase + kColO;
     const int m_local = row / p.G;
     const int g = row - m_local * p.G;
-    uint32_t sph[2] = {0, 0}, oph = 0, pv_seen = 0;  // pv_seen: P.V products of this tile so far
+    uint32_t sph = 0, oph = 0, pv_seen = 0;  // sph bit b: parity on s_full[t][b]; pv_seen: P.V products so far
     bool ok = true;
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
@@ -376,11 +390,11 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       int j = 0;
       for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks), ++j) {
         // warp-uniform outcome: the TMEM accesses below are warp-collective
-        if (!__all_sync(kFullMask, bounded_wait(&bars->s_full[t][j & 1], sph[j & 1], abort_flag))) {
+        if (!__all_sync(kFullMask, bounded_wait(&bars->s_full[t][j & 1], (sph >> (j & 1)) & 1u, abort_flag))) {
           ok = false;
           break;
         }
-        sph[j & 1] ^= 1;
+        sph ^= 1u << (j & 1);
         tc_fence_after();
         if (warp_active) {
           const int c0 = c * kChunk;
@@ -393,39 +407,48 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           float sv[kChunk / 32][32];
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) tmem_ld32(tS + 32 * gq, sv[gq]);
-          // This row's visible keys within each 32-key group, as a bit mask
-          // (visible set [0, ds) U [de, e2)), and the warp-uniform classes
-          // "every row sees all 32 keys" / "no row sees any".
+          // Warp-uniform class of each 32-key group: every lane's row sees all
+          // 32 keys (no mask arithmetic) or none of them (no exp); otherwise
+          // this row's visible keys (set [0, ds) U [de, e2)) as a bit mask.
           uint32_t vmask[kChunk / 32];
           uint32_t full_bits = 0, none_bits = 0;
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             const int g0 = c0 + 32 * gq;
-            auto low = [](int n) -> uint32_t {
-              return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
-            };
-            uint32_t vm = low(p.ds - g0) | (low(e2 - g0) & ~low(p.de - g0));
-            if (32 * gq >= ncols) vm = 0u;
+            const bool in_chunk = 32 * gq < ncols;
+            const bool full = in_chunk && ((g0 + 32 <= p.ds) || (g0 >= p.de && g0 + 32 <= e2));
+            const bool none = !in_chunk || ((g0 >= p.ds) && (g0 + 32 <= p.de || g0 >= e2));
+            full_bits |= (__all_sync(kFullMask, full) ? 1u : 0u) << gq;
+            none_bits |= (__all_sync(kFullMask, none) ? 1u : 0u) << gq;
+            uint32_t vm = 0u;
+            if (!(((full_bits | none_bits) >> gq) & 1u)) {
+              auto low = [](int n) -> uint32_t {
+                return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+              };
+              vm = low(p.ds - g0) | (low(e2 - g0) & ~low(p.de - g0));
+            }
             vmask[gq] = vm;
-            full_bits |= (__all_sync(kFullMask, vm == 0xffffffffu) ? 1u : 0u) << gq;
-            none_bits |= (__all_sync(kFullMask, vm == 0u) ? 1u : 0u) << gq;
           }
           tmem_wait_ld();
-          float mx = -INFINITY;
+          // row max with four independent accumulators (short dependency chains)
+          float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             if ((none_bits >> gq) & 1u) continue;
             if ((full_bits >> gq) & 1u) {
 #pragma unroll
-              for (int i = 0; i < 32; i += 2) mx = fmax3(mx, sv[gq][i], sv[gq][i + 1]);
+              for (int i = 0; i < 32; i += 2)
+                mxa[(i >> 1) & 3] = fmax3(mxa[(i >> 1) & 3], sv[gq][i], sv[gq][i + 1]);
             } else {
               const uint32_t vm = vmask[gq];
 #pragma unroll
               for (int i = 0; i < 32; i += 2)
-                mx = fmax3(mx, ((vm >> i) & 1u) ? sv[gq][i] : -INFINITY,
-                           ((vm >> (i + 1)) & 1u) ? sv[gq][i + 1] : -INFINITY);
+                mxa[(i >> 1) & 3] = fmax3(mxa[(i >> 1) & 3],
+                                          ((vm >> i) & 1u) ? sv[gq][i] : -INFINITY,
+                                          ((vm >> (i + 1)) & 1u) ? sv[gq][i + 1] : -INFINITY);
             }
           }
+          const float mx = fmax3(fmaxf(mxa[0], mxa[1]), mxa[2], mxa[3]);
           const float mz = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
           // The reference max moves only when this chunk's max exceeds it by
           // more than the threshold; O and l are then rescaled by alpha (after
@@ -442,12 +465,13 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
             }
           }
           // P = exp2(s * scale_log2 - mref) as bf16 pairs into TMEM. Key pairs
-          // go through the f32x2 FMA pipe; most exps run on MUFU, one pair in
-          // kPolyEvery on the FMA pipe (full groups only, where no -inf occurs).
+          // go through the f32x2 FMA pipe; exps run on MUFU except for the pairs
+          // kPolyMask selects, which use the FMA-pipe polynomial (full groups
+          // only, where no -inf occurs).
           const float nref = (m_run == -INFINITY) ? 0.f : -m_run;
           const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2);
           const uint64_t nr2 = f2_pack(nref, nref);
-          uint64_t acc = f2_pack(0.f, 0.f);
+          uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // four (+0.f, +0.f) pairs
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             if (32 * gq >= ncols) continue;
@@ -462,12 +486,12 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
                 uint64_t e;
                 float x0, x1;
                 f2_unpack(x, x0, x1);
-                if (k % kPolyEvery == kPolyEvery - 1) {
+                if ((kPolyMask >> (k & 7)) & 1u) {
                   e = f2_exp2_poly(f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f)));
                 } else {
                   e = f2_pack(ex2(x0), ex2(x1));
                 }
-                acc = f2_add(acc, e);
+                acc[k & 3] = f2_add(acc[k & 3], e);
                 float e0, e1;
                 f2_unpack(e, e0, e1);
                 pk[k] = pack_bf16x2(e0, e1);
@@ -481,14 +505,14 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
                 f2_unpack(x, x0, x1);
                 const float e0 = ((vm >> (2 * k)) & 1u) ? ex2(x0) : 0.f;
                 const float e1 = ((vm >> (2 * k + 1)) & 1u) ? ex2(x1) : 0.f;
-                acc = f2_add(acc, f2_pack(e0, e1));
+                acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
                 pk[k] = pack_bf16x2(e0, e1);
               }
             }
             tmem_st16(tP + 16 * gq, pk);
           }
           float acc0, acc1;
-          f2_unpack(acc, acc0, acc1);
+          f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), acc0, acc1);
           const float lsum = acc0 + acc1;
           l_run = l_run * alpha + lsum;
           tmem_wait_st();
@@ -517,10 +541,16 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         if (lane == 0) mbar_arrive(&bars->p_full[t][j & 1]);
       }
       if (!ok) break;
-      // epilogue: O / l -> bf16 rows of o
+      // epilogue: O / l -> bf16 rows, staged in shared memory (128B-swizzled,
+      // the layout of the output tensor map) and written by one TMA store
       if (!__all_sync(kFullMask, bounded_wait(&bars->o_full[t], oph, abort_flag))) { ok = false; break; }
       oph ^= 1;
       tc_fence_after();
+      uint8_t* stage = o_smem + t * kTileBytes;
+      const bool leader = (quarter == 0 && lane == 0);
+      // the previous store from this staging tile must have read it
+      if (leader) bulk_wait_read0();
+      named_barrier(1 + t, 128);
       if (warp_active) {
         float o[2][32];
         if (j > 0) {
@@ -531,9 +561,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         if (valid) {
           const bool any = l_run > 0.f;
           const float inv = any ? 1.f / l_run : 0.f;
-          __nv_bfloat16* orow = p.o + static_cast<long long>(it.b) * p.o_sb +
-                                static_cast<long long>(m) * p.o_sm +
-                                static_cast<long long>(it.kvh * p.G + g) * p.o_sh;
+          uint8_t* srow = stage + row * kRowBytes;
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
             uint32_t w[4];
@@ -543,12 +571,20 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
               const float b = any ? o[v >> 2][(v & 3) * 8 + 2 * e + 1] * inv : 0.f;
               w[e] = pack_bf16x2(a, b);
             }
-            reinterpret_cast<uint4*>(orow)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(srow + ((v ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
+      fence_proxy_async_smem();
       tc_fence_before();
+      named_barrier(1 + t, 128);
+      if (leader) {
+        tma_store_4d(&p.tm_o, stage, 0, it.kvh * p.G, m_first, it.b);
+        bulk_commit_group();
+      }
     }
+    // stores must finish reading shared memory before the CTA exits
+    if (quarter == 0 && lane == 0) bulk_wait_all0();
   }
 
   tc_fence_before();
@@ -697,6 +733,9 @@ static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
   if (st != VLAK_OK) return st;
   st = encode_map(&prm.tm_v, a->v, a->Hkv, a->N, a->B, a->v_stride[2], a->v_stride[1],
                   a->v_stride[0], 1, kChunk, "v");
+  if (st != VLAK_OK) return st;
+  st = encode_map(&prm.tm_o, a->o, a->H, a->M, a->B, a->o_stride[2], a->o_stride[1],
+                  a->o_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "o");
   if (st != VLAK_OK) return st;
 
   // One-time per-device opt-in to the large dynamic shared-memory carve-out.

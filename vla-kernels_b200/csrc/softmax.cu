@@ -164,12 +164,6 @@ __device__ __forceinline__ void ml_update(float& m, float& l, float x) {
   l = l * expf(m - mn) + expf(x - mn);
   m = mn;
 }
-__device__ __forceinline__ void ml_merge(float& m, float& l, float mo, float lo) {
-  const float mn = fmaxf(m, mo);
-  if (mn == -INFINITY) return;
-  l = l * expf(m - mn) + lo * expf(mo - mn);
-  m = mn;
-}
 
 template <typename T, int NT, bool kVector, class Group>
 __device__ __forceinline__ void row_softmax_stream(const T* __restrict__ xr, T* __restrict__ yr,
