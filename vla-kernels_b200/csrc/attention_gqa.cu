@@ -75,20 +75,22 @@ constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s per wait
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
                                              volatile int* abort_flag,
                                              bool honour_abort = true) {
-  // each try suspends the thread in hardware for up to 20 us while the phase
-  // is incomplete; the elapsed time is checked between tries
+  // each try may suspend the thread in hardware while the phase is
+  // incomplete; the elapsed time is checked every 64 tries
   if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
   uint64_t t0;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  for (;;) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
-    if (honour_abort && *abort_flag) return false;
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (t - t0 > kWaitLimitNs) {
-      record_device_error(VLAK_ERR_DEVICE_TIMEOUT);
-      *abort_flag = 1;
-      return false;
+    if ((it & 63u) == 0) {
+      if (honour_abort && *abort_flag) return false;
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > kWaitLimitNs) {
+        record_device_error(VLAK_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }
@@ -142,7 +144,8 @@ struct Barriers {
   uint64_t kv_full[kStages], kv_empty[kStages];
   // S and P are double-buffered per tile; each buffer has its own pair of
   // barriers, so no barrier ever runs two phases ahead of its waiter
-  uint64_t s_full[2][2], p_full[2][2];  // [tile][buffer]
+  uint64_t s_full[2][2];  // [tile][buffer]
+  uint64_t p_full[2];     // [buffer]: every softmax warp of the item's tiles arrives
   uint64_t pv_done[2], o_full[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -206,10 +209,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->q_full[i], 1);
       mbar_init(&bars->q_empty[i], 1);
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&bars->s_full[i][b], 1);
-        mbar_init(&bars->p_full[i][b], 4);  // one arrival per softmax warp
-      }
+      for (int b = 0; b < 2; ++b) mbar_init(&bars->s_full[i][b], 1);
+      mbar_init(&bars->p_full[i], 8);  // one arrival per softmax warp of both tiles
       mbar_init(&bars->pv_done[i], 1);
       mbar_init(&bars->o_full[i], 1);
     }
@@ -238,59 +239,71 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
 
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------ producer
+    // The whole warp runs this loop (converged); one elected lane issues.
     if (lane == 0) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
       prefetch_tmap(&p.tm_o);
-      uint32_t qi = 0, kv = 0;
-      // per full barrier: bit i of *_used = armed at least once, bit i of
-      // *_par = parity of its most recently armed phase (registers, no arrays)
-      uint32_t q_used = 0, q_par = 0, kv_used = 0, kv_par = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
-        const Item it = decode_item(p, item);
-        const int qs = qi & 1;
-        if (!bounded_wait(&bars->q_empty[qs], ((qi >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
-        mbar_arrive_expect_tx(&bars->q_full[qs], qbytes);
-        q_par = (q_used & (1u << qs)) ? (q_par ^ (1u << qs)) : q_par;
-        q_used |= 1u << qs;
-        for (int t = 0; t < it.tiles_active; ++t)
-          tma_load_4d(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
-                      it.kvh * p.G, it.m0 + t * p.MT, it.b);
-        for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks)) {
-          const int s = kv % kStages;
-          if (!bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kChunkBytes);
-          kv_par = (kv_used & (1u << s)) ? (kv_par ^ (1u << s)) : kv_par;
-          kv_used |= 1u << s;
-          tma_load_4d(k_smem + s * kChunkBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
-          tma_load_4d(v_smem + s * kChunkBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
-          ++kv;
-        }
-      }
-      // never leave the CTA with copies in flight: wait for the last phase
-      // armed on every full barrier (bounded, independent of the abort flag)
-      for (int i = 0; i < 2; ++i)
-        if (q_used & (1u << i)) bounded_wait(&bars->q_full[i], (q_par >> i) & 1u, abort_flag, false);
-      for (int s = 0; s < kStages; ++s)
-        if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
     }
-    __syncwarp();  // reconverge before the CTA-wide barrier
+    __syncwarp();
+    uint32_t qi = 0, kv = 0;
+    // per full barrier: bit i of *_used = armed at least once, bit i of
+    // *_par = parity of its most recently armed phase (registers, no arrays)
+    uint32_t q_used = 0, q_par = 0, kv_used = 0, kv_par = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
+      const Item it = decode_item(p, item);
+      const int qs = qi & 1;
+      if (!__all_sync(kFullMask, bounded_wait(&bars->q_empty[qs], ((qi >> 1) & 1) ^ 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
+      mbar_arrive_expect_tx_elect(&bars->q_full[qs], qbytes);
+      q_par = (q_used & (1u << qs)) ? (q_par ^ (1u << qs)) : q_par;
+      q_used |= 1u << qs;
+      for (int t = 0; t < it.tiles_active; ++t)
+        tma_load_4d_elect(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
+                          it.kvh * p.G, it.m0 + t * p.MT, it.b);
+      for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks)) {
+        const int s = kv % kStages;
+        if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx_elect(&bars->kv_full[s], 2 * kChunkBytes);
+        kv_par = (kv_used & (1u << s)) ? (kv_par ^ (1u << s)) : kv_par;
+        kv_used |= 1u << s;
+        tma_load_4d_elect(k_smem + s * kChunkBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+        tma_load_4d_elect(v_smem + s * kChunkBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+        ++kv;
+      }
+    }
+    // never leave the CTA with copies in flight: wait for the last phase
+    // armed on every full barrier (bounded, independent of the abort flag)
+    for (int i = 0; i < 2; ++i)
+      if (q_used & (1u << i)) bounded_wait(&bars->q_full[i], (q_par >> i) & 1u, abort_flag, false);
+    for (int s = 0; s < kStages; ++s)
+      if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
+    __syncwarp();
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     // Per item, chunk j of tile t:  S_t(j) -> buffer j%2 (issued two chunks
     // ahead), then, once softmax has turned it into P_t(j) (buffer j%2),
     // O_t (+)= P_t(j) V(j). Issue order per chunk: PV_t(j) then S_t(j+2), so
     // the commit of S_t(j+2) also covers PV_t(j) (same thread, in order).
-    if (lane == 0) {
-      uint32_t qi = 0, kv = 0, pph = 0;  // bit 2t+b: parity expected on p_full[t][b]
+    // The whole warp runs the loop (converged); one elected lane issues.
+    {
+      uint32_t qi = 0, kv = 0, pph = 0;  // bit b: parity expected on p_full[b]
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
         const Item it = decode_item(p, item);
         const int qs = qi & 1;
-        if (!bounded_wait(&bars->q_full[qs], (qi >> 1) & 1, abort_flag)) { ok = false; break; }
+        if (!__all_sync(kFullMask, bounded_wait(&bars->q_full[qs], (qi >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t q_base = smem_u32(q_smem + qs * 2 * kTileBytes);
         auto issue_s = [&](int t, int c, int j) {
@@ -301,8 +314,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           const uint32_t d = tmem + t * kTileCols + kColS + (j & 1) * kChunk;
 #pragma unroll
           for (int k = 0; k < 4; ++k)  // head_dim 64 = 4 x K16, 32 B apart in a swizzled row
-            umma_ss(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0);
-          umma_commit(&bars->s_full[t][j & 1]);
+            umma_ss_elect(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0);
+          umma_commit_elect(&bars->s_full[t][j & 1]);
         };
         auto issue_pv = [&](int t, int c, int j) {
           const int s = (kv + j) % kStages;
@@ -312,23 +325,24 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           const uint32_t a = tmem + t * kTileCols + kColP + (j & 1) * (kChunk / 2);
           const uint32_t d = tmem + t * kTileCols + kColO;
           for (int k = 0; k < ncols / 16; ++k)  // 16 keys = 8 packed columns of P, 2 KB of V
-            umma_ts(d, a + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc, (j > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&bars->pv_done[t]);
+            umma_ts_elect(d, a + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit_elect(&bars->pv_done[t]);
         };
         auto wait_kv = [&](int j) {
           const uint32_t n = kv + j;
-          if (!bounded_wait(&bars->kv_full[n % kStages], (n / kStages) & 1, abort_flag)) return false;
+          if (!__all_sync(kFullMask, bounded_wait(&bars->kv_full[n % kStages], (n / kStages) & 1, abort_flag)))
+            return false;
           tc_fence_after();
           return true;
         };
-        auto wait_p = [&](int t, int j) {
-          const uint32_t bit = 1u << (2 * t + (j & 1));
-          if (!bounded_wait(&bars->p_full[t][j & 1], (pph & bit) ? 1u : 0u, abort_flag)) return false;
+        auto wait_p = [&](int j) {
+          const uint32_t bit = 1u << (j & 1);
+          if (!__all_sync(kFullMask, bounded_wait(&bars->p_full[j & 1], (pph & bit) ? 1u : 0u, abort_flag)))
+            return false;
           pph ^= bit;
           tc_fence_after();
           return true;
         };
-
         int cur = next_live(p, it, 0, n_chunks);
         int nxt = cur >= 0 ? next_live(p, it, cur + 1, n_chunks) : -1;
         int j = 0;
@@ -342,25 +356,27 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         }
         while (cur >= 0) {
           const int nn = nxt >= 0 ? next_live(p, it, nxt + 1, n_chunks) : -1;  // chunk j+2
-          if (nn >= 0 && !wait_kv(j + 2)) { ok = false; break; }
-          for (int t = 0; t < it.tiles_active; ++t) {
-            if (!wait_p(t, j)) { ok = false; break; }
-            issue_pv(t, cur, j);
-            if (nn >= 0) issue_s(t, nn, j + 2);
+          // one wait for both tiles' P, then one burst: PV of every tile
+          // first (so the next chunk's softmax inputs are not delayed), then
+          // the S two chunks ahead
+          if (!wait_p(j)) { ok = false; break; }
+          for (int t = 0; t < it.tiles_active; ++t) issue_pv(t, cur, j);
+          if (nn >= 0) {
+            if (!wait_kv(j + 2)) { ok = false; break; }
+            for (int t = 0; t < it.tiles_active; ++t) issue_s(t, nn, j + 2);
           }
-          if (!ok) break;
-          umma_commit(&bars->kv_empty[(kv + j) % kStages]);
+          umma_commit_elect(&bars->kv_empty[(kv + j) % kStages]);
           cur = nxt;
           nxt = nn;
           ++j;
         }
         if (!ok) break;
-        for (int t = 0; t < it.tiles_active; ++t) umma_commit(&bars->o_full[t]);
-        umma_commit(&bars->q_empty[qs]);
+        for (int t = 0; t < it.tiles_active; ++t) umma_commit_elect(&bars->o_full[t]);
+        umma_commit_elect(&bars->q_empty[qs]);
         kv += j;
       }
       // every issued MMA must complete before TMEM is released
-      umma_commit(&bars->drain);
+      umma_commit_elect(&bars->drain);
       bounded_wait(&bars->drain, 0, abort_flag, false);
     }
     __syncwarp();  // reconverge before the CTA-wide barrier and the dealloc
@@ -372,7 +388,6 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + t * kTileCols;
     const uint32_t tO = tbase + kColO;
     const int m_local = row / p.G;
-    const int g = row - m_local * p.G;
     uint32_t sph = 0, oph = 0, pv_seen = 0;  // sph bit b: parity on s_full[t][b]; pv_seen: P.V products so far
     bool ok = true;
 
@@ -537,8 +552,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         }
         ++pv_seen;
         tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->p_full[t][j & 1]);
+        // eight arrivals complete a phase; with one active tile its warps
+        // arrive for the absent ones too
+        mbar_arrive_elect(&bars->p_full[j & 1], it.tiles_active == 2 ? 1u : 2u);
       }
       if (!ok) break;
       // epilogue: O / l -> bf16 rows, staged in shared memory (128B-swizzled,
@@ -552,26 +568,26 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       if (leader) bulk_wait_read0();
       named_barrier(1 + t, 128);
       if (warp_active) {
-        float o[2][32];
-        if (j > 0) {
-          tmem_ld32(tO, o[0]);
-          tmem_ld32(tO + 32, o[1]);
-          tmem_wait_ld();
-        }
-        if (valid) {
-          const bool any = l_run > 0.f;
-          const float inv = any ? 1.f / l_run : 0.f;
-          uint8_t* srow = stage + row * kRowBytes;
+        const bool any = (j > 0) && (l_run > 0.f);
+        const float inv = any ? 1.f / l_run : 0.f;
+        uint8_t* srow = stage + row * kRowBytes;
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            uint32_t w[4];
+        for (int half = 0; half < 2; ++half) {  // 32 columns of O at a time
+          float o[32];
+          if (j > 0) {
+            tmem_ld32(tO + 32 * half, o);
+            tmem_wait_ld();
+          }
+          if (valid) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float a = any ? o[v >> 2][(v & 3) * 8 + 2 * e] * inv : 0.f;
-              const float b = any ? o[v >> 2][(v & 3) * 8 + 2 * e + 1] * inv : 0.f;
-              w[e] = pack_bf16x2(a, b);
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                w[e] = any ? pack_bf16x2(o[v * 8 + 2 * e] * inv, o[v * 8 + 2 * e + 1] * inv) : 0u;
+              const int cv = half * 4 + v;  // 16-byte chunk of the 128-byte row
+              *reinterpret_cast<uint4*>(srow + ((cv ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            *reinterpret_cast<uint4*>(srow + ((v ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
       }
