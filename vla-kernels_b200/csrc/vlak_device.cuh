@@ -208,6 +208,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking probe of the phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // As mbar_try_wait, but the thread may be suspended in hardware (up to
 // `suspend_ns`) until the phase completes instead of returning at once, so a
 // waiting warp stops taking issue slots.
@@ -321,33 +333,41 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // Warp-converged issue: the whole warp executes these, one elected lane
-// issues the instruction (keeps operands in uniform registers).
+// issues the instruction (keeps operands in uniform registers). `on` predicates
+// the issue inside the asm: a burst of MMAs written as straight-line code with
+// predicates issues at the tensor pipe's rate, while a branch (or loop
+// back-edge) between consecutive MMAs adds tens of cycles to each.
 __device__ __forceinline__ void umma_ss_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
+                                              uint32_t idesc, uint32_t accumulate,
+                                              uint32_t on = 1u) {
   asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
+      "{\n\t.reg .pred e, p, q;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      "setp.ne.and.b32 q, %5, 0, e;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(on)
       : "memory");
 }
 __device__ __forceinline__ void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
+                                              uint32_t idesc, uint32_t accumulate,
+                                              uint32_t on = 1u) {
   asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
+      "{\n\t.reg .pred e, p, q;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      "setp.ne.and.b32 q, %5, 0, e;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(on)
       : "memory");
 }
-__device__ __forceinline__ void umma_commit_elect(uint64_t* bar) {
+__device__ __forceinline__ void umma_commit_elect(uint64_t* bar, uint32_t on = 1u) {
   asm volatile(
-      "{\n\t.reg .pred e;\n\t"
+      "{\n\t.reg .pred e, q;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
-          smem_u32(bar))
+      "setp.ne.and.b32 q, %1, 0, e;\n\t"
+      "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar)), "r"(on)
       : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_expect_tx_elect(uint64_t* bar, uint32_t bytes) {
