@@ -44,6 +44,7 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 from kernels import workloads as wl  # noqa: E402
+from kernels.batch_shard import shard  # noqa: E402
 
 GLOBAL_B = 2048
 LAYERS, FLOW_STEPS = 16, 10
@@ -161,13 +162,6 @@ def barrier(world: int):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-
-
-def shard(B: int, rank: int, world: int) -> tuple[int, int]:
-    """Contiguous batch shard of rank `rank`: [lo, hi)."""
-    base, rem = divmod(B, world)
-    lo = rank * base + min(rank, rem)
-    return lo, lo + base + (1 if rank < rem else 0)
 
 
 # ---------------------------------------------------------------- our arm

@@ -137,6 +137,14 @@ VLAK_API int vlak_attn_gqa_v4_fwd(const vlak_attn_gqa_args* args, void* stream);
 VLAK_API int vlak_attn_gqa_check(const vlak_attn_gqa_args* args, int64_t* prefix_out,
                         float* scale_out);
 
+/* Self-test of the bounded device waits. No counterpart in the reference:
+ * a test hook for the failure path that replaces a hang. Launches, on
+ * `stream`, one kernel that waits on a barrier nothing completes; after the
+ * 1 s wait limit it records VLAK_ERR_DEVICE_TIMEOUT in the device error word
+ * (read it with vlak_device_error_read) and returns, leaving the context
+ * usable. */
+VLAK_API int vlak_selftest_wait_timeout(void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -20,6 +20,7 @@ VLAK_OK = 0
 VLAK_ERR_INVALID_ARGUMENT = 1
 VLAK_ERR_ALIGNMENT = 2
 VLAK_ERR_UNSUPPORTED_DTYPE = 3
+VLAK_ERR_DEVICE_TIMEOUT = 5
 DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
 
 
@@ -47,6 +48,7 @@ def lib():
     L.vlak_attn_gqa_check.argtypes = [ctypes.POINTER(GqaArgs), ctypes.POINTER(ctypes.c_int64),
                                       ctypes.POINTER(ctypes.c_float)]
     L.vlak_device_error_read.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    L.vlak_selftest_wait_timeout.argtypes = [ctypes.c_void_p]
     return L
 
 

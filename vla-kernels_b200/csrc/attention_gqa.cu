@@ -797,7 +797,39 @@ static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
   return VLAK_OK;
 }
 
+namespace {
+
+// Self-test of the bounded-wait machinery: one thread waits on an mbarrier
+// that nothing arrives on. The wait runs out after its limit, records
+// VLAK_ERR_DEVICE_TIMEOUT in the device error word and the kernel returns
+// normally, so the context stays usable.
+__global__ void wait_timeout_selftest() {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) bounded_wait(&bar, 0, &abort_flag);
+}
+
+}  // namespace
+
+int selftest_wait_timeout(void* stream) {
+  clear_error();
+  wait_timeout_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("wait_timeout_selftest launch failed", e);
+  return VLAK_OK;
+}
+
 }  // namespace vlak
+
+extern "C" int vlak_selftest_wait_timeout(void* stream) {
+  return vlak::selftest_wait_timeout(stream);
+}
 
 extern "C" int vlak_attn_gqa_check(const vlak_attn_gqa_args* args, int64_t* prefix_out,
                                    float* scale_out) {
