@@ -42,7 +42,7 @@ enum {
 };
 
 /* element types */
-enum { VLAK_F32 = 0, VLAK_F16 = 1, VLAK_BF16 = 2, VLAK_F64 = 3 };
+enum { VLAK_F32 = 0, VLAK_F16 = 1, VLAK_BF16 = 2, VLAK_F64 = 3, VLAK_I32 = 4, VLAK_I64 = 5 };
 
 /* Library identity and diagnostics. */
 VLAK_API int vlak_abi_version(void);
@@ -136,6 +136,39 @@ VLAK_API int vlak_attn_gqa_v4_fwd(const vlak_attn_gqa_args* args, void* stream);
  * arguments; writes the resolved values when the pointers are non-NULL. */
 VLAK_API int vlak_attn_gqa_check(const vlak_attn_gqa_args* args, int64_t* prefix_out,
                         float* scale_out);
+
+/* GQA attention with a per-sample length mask (varlen prefix attention, the
+ * reference's C4 site, which it leaves on SDPA; no counterpart kernel there,
+ * new schema vlak::fused_attention_gqa_varlen). Same arguments as
+ * vlak_attn_gqa_fwd; prefix_len / dead_start / dead_end are ignored.
+ *   lengths       : device array of B lengths, VLAK_I32 or VLAK_I64
+ *   visible(r, c) = c < L_b && r < L_b, with L_b clamped to [0, N];
+ *   rows r >= L_b are written as zeros. */
+VLAK_API int vlak_attn_gqa_varlen_fwd(const vlak_attn_gqa_args* args, const void* lengths,
+                                      int lengths_dtype, void* stream);
+
+/* GQA attention with a bool mask (B, M, N) broadcast over heads, on the
+ * tensor cores. Serves the bf16 tensor-mask path of vlak::fused_attention
+ * (the reference's v2, kernels/attention/fused_attention.cu:555-577).
+ * Same arguments as vlak_attn_gqa_fwd; the analytic fields are ignored.
+ *   mask           : device bytes, nonzero = attend; keys contiguous
+ *   mask_stride_b/m: byte strides of dims b and m (0 broadcasts) */
+VLAK_API int vlak_attn_gqa_masked_fwd(const vlak_attn_gqa_args* args, const void* mask,
+                                      int64_t mask_stride_b, int64_t mask_stride_m,
+                                      void* stream);
+
+/* Non-GQA attention on the CUDA cores with fp32 math: the v1 path of
+ * vlak::fused_attention for fp32 / fp16 / fp64 inputs (replaces
+ * fused_attention_warp_row and its host branch,
+ * kernels/attention/fused_attention.cu:28-79, :578-592).
+ *   q, o : (B, H, M, 64) contiguous; k, v : (B, H, N, 64) contiguous
+ *   dtype: VLAK_F32 / VLAK_F16 / VLAK_BF16 / VLAK_F64
+ *   mask : optional bool (B, M, N) contiguous, broadcast over heads (NULL = none)
+ *   scale: <= 0 selects 1/sqrt(64)
+ * A row with no visible key is written as zeros. */
+VLAK_API int vlak_attn_fwd(const void* q, const void* k, const void* v, void* o, int dtype,
+                           int64_t B, int64_t H, int64_t M, int64_t N, const void* mask,
+                           double scale, void* stream);
 
 /* Self-test of the bounded device waits. No counterpart in the reference:
  * a test hook for the failure path that replaces a hang. Launches, on

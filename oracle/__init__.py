@@ -16,5 +16,9 @@ from .attention_oracle import (  # noqa: F401
     analytic_visible,
     gqa_attention,
     gqa_attention_torch_cpu,
+    gqa_attention_varlen,
+    masked_attention,
+    sdpa_bhmd,
     solve_analytic_params,
+    varlen_visible,
 )

@@ -21,6 +21,13 @@ Fixtures:
   masks_golden.npz     the three masks of results/real_masks.pt (packed bits)
                        and what _analytic_params (vla/variants.py:236-255)
                        solves them to
+  sdpa_golden.npz      ref_sdpa outputs (tests/test_attention.py:25-30) for the
+                       (B, H, M, 64) op: the SmolVLA prefix/causal pattern of
+                       smolvla_mask (:33-40), the real 241x241 prefix mask
+                       (pad rows and a block-causal state token), a random mask
+                       and no mask; fully masked rows are NaN there
+  varlen_golden.npz    ref_sdpa outputs for per-sample lengths (the C4 prefix
+                       site), GQA by repeating kv heads as ref_attn does
 """
 from __future__ import annotations
 
@@ -44,6 +51,54 @@ ATTN_CASES = [
     (1, 40, 128, 6, 2, 128, 32, 64, 5),      # dead band covers 2 fragments
     (1, 12, 16, 2, 1, 12, 0, 12, 6),         # rows 0-7 see no key
 ]
+
+
+# (B, H, M, N, mask kind, seed) for the (B, H, M, 64) op
+SDPA_CASES = [
+    (1, 3, 50, 291, "smolvla241", 10),
+    (2, 2, 33, 65, "smolvla32", 11),
+    (1, 2, 241, 241, "real_prefix", 12),
+    (2, 2, 17, 33, "random", 13),
+    (1, 2, 40, 70, "none", 14),
+]
+# (B, M, N, H, Hkv, lengths, seed) for per-sample lengths
+VARLEN_CASES = [
+    (2, 241, 241, 3, 1, (150, 241), 20),
+    (2, 40, 40, 3, 1, (0, 17), 21),
+]
+
+
+def smolvla_pattern(M, N, prefix):
+    """The prefix-bidirectional + causal-suffix pattern of smolvla_mask
+    (tests/test_attention.py:33-40), built on the CPU."""
+    m = torch.zeros(M, N, dtype=torch.bool)
+    m[:, :prefix] = True
+    start = N - M
+    for i in range(M):
+        m[i, prefix:start + i + 1] = True
+    return m
+
+
+def sdpa_mask(kind, B, M, N, seed, real_masks):
+    if kind == "none":
+        return None
+    if kind.startswith("smolvla"):
+        return smolvla_pattern(M, N, int(kind[len("smolvla"):]))[None].expand(B, M, N).contiguous()
+    if kind == "real_prefix":
+        return real_masks[(M, N)][None].expand(B, M, N).contiguous()
+    g = torch.Generator().manual_seed(seed + 1000)
+    m = torch.rand(B, M, N, generator=g) < 0.6
+    m[0, 3] = False  # one row sees no key
+    return m
+
+
+def bhmd_inputs(B, H, M, N, seed):
+    """Seeded bf16-valued q/k/v in (B, H, seq, 64), held as fp32."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, M, 64, generator=g).to(torch.bfloat16).float()
+    k = torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).float()
+    v = torch.randn(B, H, N, 64, generator=g).to(torch.bfloat16).float()
+    return q, k, v
 
 
 def attn_inputs(B, M, N, H, Hkv, seed):
@@ -86,6 +141,7 @@ def main():
     sys.path.insert(0, a.reference)
     from tests.test_attention_gqa import ref_attn  # reference oracle
     from vla.variants import _analytic_params      # reference mask solver
+    from tests.test_attention import ref_sdpa       # reference SDPA oracle
 
     # ---- softmax
     out = {}
@@ -114,7 +170,34 @@ def main():
         par = _analytic_params(m.cpu(), M, N)
         out[f"{key}__params"] = np.array(par if par is not None else (-1, -1, -1))
     np.savez_compressed(os.path.join(HERE, "masks_golden.npz"), **out)
-    for f in ("softmax_golden.npz", "attention_golden.npz", "masks_golden.npz"):
+
+    # ---- (B, H, M, 64) op with bool / pattern / no masks
+    real = {tuple(m.shape): m.cpu().bool() for m in masks.values()}
+    out = {}
+    for i, (B, H, M, N, kind, seed) in enumerate(SDPA_CASES):
+        q, k, v = bhmd_inputs(B, H, M, N, seed)
+        mask = sdpa_mask(kind, B, M, N, seed, real)
+        out[f"s{i}__out"] = ref_sdpa(q, k, v, mask).numpy()
+        out[f"s{i}__sha256"] = np.array(digest(q, k, v))
+        if mask is not None:
+            out[f"s{i}__mask"] = np.packbits(mask.numpy().astype(np.uint8).ravel())
+    np.savez_compressed(os.path.join(HERE, "sdpa_golden.npz"), **out)
+
+    # ---- per-sample lengths (GQA, natural layouts)
+    out = {}
+    for i, (B, M, N, H, Hkv, lengths, seed) in enumerate(VARLEN_CASES):
+        q, k, v = attn_inputs(B, M, N, H, Hkv, seed)
+        L = torch.tensor(lengths)[:, None, None]
+        vis = (torch.arange(N)[None, None, :] < L) & (torch.arange(M)[None, :, None] < L)
+        G = H // Hkv
+        qh = q.float().transpose(1, 2)
+        kh = k.float().transpose(1, 2).repeat_interleave(G, dim=1)
+        vh = v.float().transpose(1, 2).repeat_interleave(G, dim=1)
+        out[f"v{i}__out"] = ref_sdpa(qh, kh, vh, vis).transpose(1, 2).numpy()
+        out[f"v{i}__sha256"] = np.array(digest(q, k, v))
+    np.savez_compressed(os.path.join(HERE, "varlen_golden.npz"), **out)
+    for f in ("softmax_golden.npz", "attention_golden.npz", "masks_golden.npz", "sdpa_golden.npz",
+              "varlen_golden.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

@@ -118,3 +118,71 @@ def test_zero_keys_give_zero_rows():
     q = np.ones((1, 2, 2, 64))
     k = np.ones((1, 0, 1, 64))
     assert np.array_equal(gqa_attention(q, k, k), np.zeros((1, 2, 2, 64)))
+
+
+# ---- the (B, H, M, 64) op and per-sample lengths (ref_sdpa fixtures)
+
+from oracle import gqa_attention_varlen, sdpa_bhmd  # noqa: E402
+from tests.golden.make_golden import SDPA_CASES, VARLEN_CASES, bhmd_inputs  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def sdpa_golden():
+    return np.load(os.path.join(GOLDEN, "sdpa_golden.npz"))
+
+
+@pytest.fixture(scope="module")
+def varlen_golden():
+    return np.load(os.path.join(GOLDEN, "varlen_golden.npz"))
+
+
+def golden_mask(g, i, B, M, N):
+    key = f"s{i}__mask"
+    if key not in g:
+        return None
+    return np.unpackbits(g[key])[: B * M * N].reshape(B, M, N).astype(bool)
+
+
+def assert_matches_nan_as_zero(out, ref, tol=1e-5):
+    nan_rows = np.isnan(ref).all(axis=-1)
+    assert np.array_equal(out[nan_rows], np.zeros_like(out[nan_rows]))
+    np.testing.assert_allclose(out[~nan_rows], ref[~nan_rows], rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("idx", range(len(SDPA_CASES)))
+def test_sdpa_oracle_matches_ref_sdpa(sdpa_golden, idx):
+    B, H, M, N, kind, seed = SDPA_CASES[idx]
+    q, k, v = bhmd_inputs(B, H, M, N, seed)
+    assert digest(q, k, v) == str(sdpa_golden[f"s{idx}__sha256"]), "input generator changed"
+    mask = golden_mask(sdpa_golden, idx, B, M, N)
+    out = sdpa_bhmd(q.numpy(), k.numpy(), v.numpy(), attn_mask=mask)
+    assert_matches_nan_as_zero(out, sdpa_golden[f"s{idx}__out"].astype(np.float64))
+
+
+def test_real_prefix_mask_has_pad_rows_and_block_causal_state(sdpa_golden):
+    idx = [c[4] for c in SDPA_CASES].index("real_prefix")
+    B, H, M, N, _, _ = SDPA_CASES[idx]
+    m = golden_mask(sdpa_golden, idx, B, M, N)[0]
+    assert (~m[196:240]).all()               # 44 pad rows see nothing
+    assert m[240, :196].all() and m[240, 240] and not m[240, 196:240].any()
+    assert solve_analytic_params(m) is None  # not expressible analytically
+
+
+@pytest.mark.parametrize("idx", [i for i, c in enumerate(SDPA_CASES) if c[4].startswith("smolvla")])
+def test_sdpa_oracle_analytic_prefix_equals_pattern_mask(sdpa_golden, idx):
+    B, H, M, N, kind, seed = SDPA_CASES[idx]
+    q, k, v = bhmd_inputs(B, H, M, N, seed)
+    mask = golden_mask(sdpa_golden, idx, B, M, N)
+    P = int(kind[len("smolvla"):])
+    a = sdpa_bhmd(q.numpy(), k.numpy(), v.numpy(), prefix_len=P)
+    b = sdpa_bhmd(q.numpy(), k.numpy(), v.numpy(), attn_mask=mask)
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("idx", range(len(VARLEN_CASES)))
+def test_varlen_oracle_matches_ref_sdpa(varlen_golden, idx):
+    B, M, N, H, Hkv, lengths, seed = VARLEN_CASES[idx]
+    q, k, v = attn_inputs(B, M, N, H, Hkv, seed)
+    assert digest(q, k, v) == str(varlen_golden[f"v{idx}__sha256"]), "input generator changed"
+    out = gqa_attention_varlen(q.float().numpy(), k.float().numpy(), v.float().numpy(), lengths)
+    assert_matches_nan_as_zero(out, varlen_golden[f"v{idx}__out"].astype(np.float64))

@@ -26,7 +26,7 @@ INCLUDE = os.path.join(REPO, "include")
 CAPI_LIB = os.path.join(LIB_DIR, "libvlak_b200.so")
 TORCH_LIB = os.path.join(LIB_DIR, "libvlak_torch.so")
 
-CU_SOURCES = ["capi.cu", "softmax.cu", "attention_gqa.cu"]
+CU_SOURCES = ["capi.cu", "softmax.cu", "attention_gqa.cu", "attention_simt.cu"]
 HEADERS = ["vlak_device.cuh", "vlak_internal.h"]
 SHIM_SOURCES = ["torch_ops.cpp"]
 

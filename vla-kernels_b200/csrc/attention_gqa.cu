@@ -151,7 +151,21 @@ struct __align__(64) Params {
   int num_items;
   int P, ds, de;
   float scale_log2;  // softmax scale * log2(e)
+  // mask mode 1: per-sample lengths (B,), int32 or int64, in device memory
+  const void* lengths;
+  int lengths_i64;
+  // mask mode 2: bool (B, M, N) broadcast over heads, keys contiguous
+  const uint8_t* mask;
+  long long mask_sb, mask_sm;  // byte strides of dims b and m
+  int mask_words;              // rows start 4-byte aligned: four keys per load
 };
+
+// Mask modes (a template parameter of the kernel, uniform per launch):
+//   0 analytic: visible(r, c) = c < P ? (c < ds || c >= de) : c <= (N - M) + r
+//   1 per-sample length L_b: visible(r, c) = c < L_b && r < L_b (L_b clamped
+//     to [0, N]); rows r >= L_b have no visible key and are written as zeros
+//   2 bool mask (B, M, N): visible(r, c) = mask[b, r, c] != 0
+constexpr int kMaskAnalytic = 0, kMaskLength = 1, kMaskBool = 2;
 
 struct Barriers {
   uint64_t q_full[2], q_empty[2];
@@ -171,8 +185,10 @@ static_assert(sizeof(Barriers) <= kBarrierBytes, "barrier block overflows its re
 struct Item {
   int b, kvh, m0;  // m0: first query position of the item
   int tiles_active;
+  int L;           // mask mode 1: length of sample b
 };
 
+template <int kMode>
 __device__ __forceinline__ Item decode_item(const Params& p, int item) {
   Item it;
   const int mblk = item % p.n_mblk;
@@ -181,28 +197,60 @@ __device__ __forceinline__ Item decode_item(const Params& p, int item) {
   it.b = bk / p.Hkv;
   it.m0 = mblk * p.tiles * p.MT;
   it.tiles_active = (p.tiles == 2 && it.m0 + p.MT < p.M) ? 2 : 1;
+  it.L = 0;
+  if (kMode == kMaskLength) {
+    const long long len = p.lengths_i64 ? static_cast<const long long*>(p.lengths)[it.b]
+                                        : static_cast<const int*>(p.lengths)[it.b];
+    it.L = static_cast<int>(min(max(len, 0LL), static_cast<long long>(p.N)));
+  }
   return it;
 }
 
 // Whether key chunk c has a visible key for some row of the item (every role
-// evaluates this identically, so all agree on the item's live chunks).
+// evaluates this identically, so all agree on the item's live chunks). A bool
+// mask is not inspected here: every chunk of its items is processed.
+template <int kMode>
 __device__ __forceinline__ bool chunk_live(const Params& p, const Item& it, int c) {
   const int c0 = c * kChunk;
+  if (kMode == kMaskBool) return true;
+  if (kMode == kMaskLength) return c0 < it.L && it.m0 < it.L;
   const int width = min(kChunk, p.N - c0);
   const int m_hi = min(p.M, it.m0 + it.tiles_active * p.MT) - 1;
   const int e2_hi = max(p.P, min(p.N, p.N - p.M + m_hi + 1));
   return (c0 < p.ds) || (c0 + width > p.de && c0 < e2_hi);
 }
+template <int kMode>
 __device__ __forceinline__ int next_live(const Params& p, const Item& it, int c, int n_chunks) {
   for (; c < n_chunks; ++c)
-    if (chunk_live(p, it, c)) return c;
+    if (chunk_live<kMode>(p, it, c)) return c;
   return -1;
+}
+
+// Bits of keys g0 .. g0+31 of one bool-mask row (bit i set when key g0 + i is
+// below N and its mask byte is nonzero).
+__device__ __forceinline__ uint32_t mask_bits32(const Params& p, const uint8_t* row, int g0) {
+  uint32_t vm = 0u;
+  if (p.mask_words && g0 + 32 <= p.N) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(row + g0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // one byte per key -> bytes 0x01 / 0x00 -> four bits gathered by a
+      // multiply (the partial products of distinct bytes never overlap)
+      const uint32_t b = __vcmpne4(__ldg(w + i), 0u) & 0x01010101u;
+      vm |= ((b * 0x01020408u) >> 24) << (4 * i);
+    }
+  } else {
+    const int n = min(32, p.N - g0);
+    for (int i = 0; i < n; ++i) vm |= (__ldg(row + g0 + i) != 0 ? 1u : 0u) << i;
+  }
+  return vm;
 }
 __device__ __forceinline__ int chunk_cols(const Params& p, int c) {
   const int width = min(kChunk, p.N - c * kChunk);
   return (width + 15) & ~15;  // MMA N must be a multiple of 16
 }
 
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
 gqa_attention_sm100(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -267,7 +315,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     uint32_t q_used = 0, q_par = 0, kv_used = 0, kv_par = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
-      const Item it = decode_item(p, item);
+      const Item it = decode_item<kMode>(p, item);
       const int qs = qi & 1;
       if (!__all_sync(kFullMask, bounded_wait(&bars->q_empty[qs], ((qi >> 1) & 1) ^ 1, abort_flag))) {
         ok = false;
@@ -280,7 +328,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       for (int t = 0; t < it.tiles_active; ++t)
         tma_load_4d_elect(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
                           it.kvh * p.G, it.m0 + t * p.MT, it.b);
-      for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks)) {
+      for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks)) {
         const int s = kv % kStages;
         if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
           ok = false;
@@ -312,7 +360,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       uint32_t qi = 0, kv = 0, pph = 0;  // bit b: parity expected on p_full[b]
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
-        const Item it = decode_item(p, item);
+        const Item it = decode_item<kMode>(p, item);
         const int qs = qi & 1;
         if (!__all_sync(kFullMask, bounded_wait(&bars->q_full[qs], (qi >> 1) & 1, abort_flag))) {
           ok = false;
@@ -370,8 +418,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           tc_fence_after();
           return true;
         };
-        int cur = next_live(p, it, 0, n_chunks);
-        int nxt = cur >= 0 ? next_live(p, it, cur + 1, n_chunks) : -1;
+        int cur = next_live<kMode>(p, it, 0, n_chunks);
+        int nxt = cur >= 0 ? next_live<kMode>(p, it, cur + 1, n_chunks) : -1;
         int j = 0;
         if (cur >= 0) {
           if (!wait_kv(0)) { ok = false; break; }
@@ -382,7 +430,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           issue_s(nxt, 1, 1u);
         }
         while (cur >= 0) {
-          const int nn = nxt >= 0 ? next_live(p, it, nxt + 1, n_chunks) : -1;  // chunk j+2
+          const int nn = nxt >= 0 ? next_live<kMode>(p, it, nxt + 1, n_chunks) : -1;  // chunk j+2
           // both waits first (both tiles' P, the K/V two chunks ahead), then
           // one branch-free burst: PV of every tile, then the S two chunks ahead
           if (!wait_p(j)) { ok = false; break; }
@@ -418,7 +466,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     bool ok = true;
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
-      const Item it = decode_item(p, item);
+      const Item it = decode_item<kMode>(p, item);
       if (t >= it.tiles_active) continue;
       const int m_first = it.m0 + t * p.MT;        // first query position of this tile
       const int m = m_first + m_local;
@@ -426,10 +474,18 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       // a warp whose rows are all invalid skips the arithmetic
       const int warp_first_m = m_first + (quarter * 32) / p.G;
       const bool warp_active = ((quarter * 32) / p.G < p.MT) && (warp_first_m < p.M);
-      const int e2 = max(p.P, min(p.N, p.N - p.M + m + 1));
+      // this row's visible set [0, ds) U [de, e2) (mask modes 0 and 1) or its
+      // bool-mask row (mode 2)
+      const int rds = kMode == kMaskAnalytic ? p.ds : 0;
+      const int rde = kMode == kMaskAnalytic ? p.de : 0;
+      const int e2 = kMode == kMaskAnalytic ? max(p.P, min(p.N, p.N - p.M + m + 1))
+                     : kMode == kMaskLength ? (m < it.L ? it.L : 0) : 0;
+      const uint8_t* mrow = nullptr;
+      if (kMode == kMaskBool && valid)
+        mrow = p.mask + static_cast<long long>(it.b) * p.mask_sb + static_cast<long long>(m) * p.mask_sm;
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
-      for (int c = next_live(p, it, 0, n_chunks); c >= 0; c = next_live(p, it, c + 1, n_chunks), ++j) {
+      for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks), ++j) {
         // warp-uniform outcome: the TMEM accesses below are warp-collective
         if (!__all_sync(kFullMask, bounded_wait<kWaitSoftmax>(&bars->s_full[t][j & 1], (sph >> (j & 1)) & 1u, abort_flag))) {
           ok = false;
@@ -448,26 +504,34 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           float sv[kChunk / 32][32];
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) tmem_ld32(tS + 32 * gq, sv[gq]);
-          // Warp-uniform class of each 32-key group: every lane's row sees all
-          // 32 keys (no mask arithmetic) or none of them (no exp); otherwise
-          // this row's visible keys (set [0, ds) U [de, e2)) as a bit mask.
+          // Warp-uniform class of each 32-key group: every valid row of the
+          // warp sees all 32 keys (no mask arithmetic) or none of them (no
+          // exp); otherwise each row's visible keys as a bit mask. Rows past
+          // the tile or past M do not vote (their outputs are discarded), so
+          // the analytic and the bool-mask form of one mask classify alike.
           uint32_t vmask[kChunk / 32];
           uint32_t full_bits = 0, none_bits = 0;
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             const int g0 = c0 + 32 * gq;
             const bool in_chunk = 32 * gq < ncols;
-            const bool full = in_chunk && ((g0 + 32 <= p.ds) || (g0 >= p.de && g0 + 32 <= e2));
-            const bool none = !in_chunk || ((g0 >= p.ds) && (g0 + 32 <= p.de || g0 >= e2));
+            auto low = [](int n) -> uint32_t {
+              return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+            };
+            bool full, none;
+            uint32_t vm = 0u;
+            if (kMode == kMaskBool) {
+              if (in_chunk && mrow != nullptr) vm = mask_bits32(p, mrow, g0);
+              full = !valid || (in_chunk && vm == 0xffffffffu);
+              none = !valid || vm == 0u;
+            } else {
+              full = !valid || (in_chunk && ((g0 + 32 <= rds) || (g0 >= rde && g0 + 32 <= e2)));
+              none = !valid || !in_chunk || ((g0 >= rds) && (g0 + 32 <= rde || g0 >= e2));
+            }
             full_bits |= (__all_sync(kFullMask, full) ? 1u : 0u) << gq;
             none_bits |= (__all_sync(kFullMask, none) ? 1u : 0u) << gq;
-            uint32_t vm = 0u;
-            if (!(((full_bits | none_bits) >> gq) & 1u)) {
-              auto low = [](int n) -> uint32_t {
-                return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
-              };
-              vm = low(p.ds - g0) | (low(e2 - g0) & ~low(p.de - g0));
-            }
+            if (kMode != kMaskBool && !(((full_bits | none_bits) >> gq) & 1u))
+              vm = valid ? (low(rds - g0) | (low(e2 - g0) & ~low(rde - g0))) : 0u;
             vmask[gq] = vm;
           }
           tmem_wait_ld();
@@ -712,13 +776,56 @@ static int validate(const vlak_attn_gqa_args* a, int64_t* P_out, float* scale_ou
   return VLAK_OK;
 }
 
-static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
+// Mask beyond the analytic form: per-sample lengths (mode 1) or a bool mask
+// (mode 2). The analytic fields of the arguments are ignored for those modes.
+struct MaskSpec {
+  int mode = kMaskAnalytic;
+  const void* lengths = nullptr;
+  int lengths_dtype = VLAK_I32;
+  const void* mask = nullptr;
+  int64_t mask_sb = 0, mask_sm = 0;
+};
+
+template <int kMode>
+static cudaError_t launch_mode(const Params& prm, int grid, cudaStream_t cs, int device) {
+  // one-time per (device, mode) opt-in to the large dynamic shared-memory carve-out
+  static std::atomic<int> ready[64];
+  if (ready[device].load() == 0) {
+    cudaError_t e = cudaFuncSetAttribute(gqa_attention_sm100<kMode>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    ready[device].store(1);
+  }
+  gqa_attention_sm100<kMode><<<grid, kThreads, kSmemBytes, cs>>>(prm);
+  return cudaGetLastError();
+}
+
+static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSpec& ms = MaskSpec()) {
   using namespace vlak;
   clear_error();
+  if (!a_in) return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: null arguments");
+  vlak_attn_gqa_args args = *a_in;
+  const vlak_attn_gqa_args* a = &args;
+  if (ms.mode != kMaskAnalytic) {
+    args.prefix_len = -1;
+    args.dead_start = args.dead_end = 0;
+  }
   int64_t P = 0;
   float scale = 0.f;
   int st = validate(a, &P, &scale);
   if (st != VLAK_OK) return st;
+  if (ms.mode == kMaskLength) {
+    if (!ms.lengths && a->B > 0) return set_error(VLAK_ERR_INVALID_ARGUMENT, "lengths must not be null");
+    if (ms.lengths_dtype != VLAK_I32 && ms.lengths_dtype != VLAK_I64)
+      return set_error(VLAK_ERR_UNSUPPORTED_DTYPE, "lengths must be int32 or int64");
+    if (reinterpret_cast<uintptr_t>(ms.lengths) % (ms.lengths_dtype == VLAK_I64 ? 8 : 4))
+      return set_error(VLAK_ERR_ALIGNMENT, "lengths must be aligned to its element size");
+  } else if (ms.mode == kMaskBool) {
+    if (!ms.mask && a->B > 0 && a->M > 0 && a->N > 0)
+      return set_error(VLAK_ERR_INVALID_ARGUMENT, "attn_mask must not be null");
+    if (ms.mask_sb < 0 || ms.mask_sm < 0)
+      return set_error(VLAK_ERR_INVALID_ARGUMENT, "attn_mask strides must be non-negative");
+  }
   if (a->B == 0 || a->M == 0) return VLAK_OK;
   // with no keys only o is touched; empty k / v may carry null pointers
   if (!a->o || (a->N > 0 && (!a->q || !a->k || !a->v)))
@@ -766,6 +873,13 @@ static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
   prm.o_sb = a->o_stride[0];
   prm.o_sm = a->o_stride[1];
   prm.o_sh = a->o_stride[2];
+  prm.lengths = ms.lengths;
+  prm.lengths_i64 = ms.lengths_dtype == VLAK_I64 ? 1 : 0;
+  prm.mask = static_cast<const uint8_t*>(ms.mask);
+  prm.mask_sb = ms.mask_sb;
+  prm.mask_sm = ms.mask_sm;
+  prm.mask_words = (reinterpret_cast<uintptr_t>(ms.mask) % 4 == 0 && ms.mask_sb % 4 == 0 &&
+                    ms.mask_sm % 4 == 0) ? 1 : 0;
 
   st = encode_map(&prm.tm_q, a->q, a->H, a->M, a->B, a->q_stride[2], a->q_stride[1],
                   a->q_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "q");
@@ -780,19 +894,11 @@ static int launch_gqa(const vlak_attn_gqa_args* a, void* stream) {
                   a->o_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "o");
   if (st != VLAK_OK) return st;
 
-  // One-time per-device opt-in to the large dynamic shared-memory carve-out.
-  static std::atomic<int> ready[64];
   if (dev.device >= 64) return set_error(VLAK_ERR_CUDA, "device ordinal out of range");
-  if (ready[dev.device].load() == 0) {
-    cudaError_t e;
-    e = cudaFuncSetAttribute(gqa_attention_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes);
-    if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa smem opt-in", e);
-    ready[dev.device].store(1);
-  }
   const int grid = static_cast<int>(std::min<long long>(items, dev.sm_count));
-  gqa_attention_sm100<<<grid, kThreads, kSmemBytes, cs>>>(prm);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = ms.mode == kMaskLength ? launch_mode<kMaskLength>(prm, grid, cs, dev.device)
+                  : ms.mode == kMaskBool ? launch_mode<kMaskBool>(prm, grid, cs, dev.device)
+                                         : launch_mode<kMaskAnalytic>(prm, grid, cs, dev.device);
   if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa launch failed", e);
   return VLAK_OK;
 }
@@ -843,6 +949,26 @@ extern "C" int vlak_attn_gqa_fwd(const vlak_attn_gqa_args* args, void* stream) {
 
 extern "C" int vlak_attn_gqa_v4_fwd(const vlak_attn_gqa_args* args, void* stream) {
   return vlak::launch_gqa(args, stream);
+}
+
+extern "C" int vlak_attn_gqa_varlen_fwd(const vlak_attn_gqa_args* args, const void* lengths,
+                                        int lengths_dtype, void* stream) {
+  vlak::MaskSpec ms;
+  ms.mode = vlak::kMaskLength;
+  ms.lengths = lengths;
+  ms.lengths_dtype = lengths_dtype;
+  return vlak::launch_gqa(args, stream, ms);
+}
+
+extern "C" int vlak_attn_gqa_masked_fwd(const vlak_attn_gqa_args* args, const void* mask,
+                                        int64_t mask_stride_b, int64_t mask_stride_m,
+                                        void* stream) {
+  vlak::MaskSpec ms;
+  ms.mode = vlak::kMaskBool;
+  ms.mask = mask;
+  ms.mask_sb = mask_stride_b;
+  ms.mask_sm = mask_stride_m;
+  return vlak::launch_gqa(args, stream, ms);
 }
 
 extern "C" int vlak_device_error_read(int* code) {

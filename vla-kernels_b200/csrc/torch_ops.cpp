@@ -5,12 +5,17 @@
 //
 // Schemas: kernels/softmax/softmax_kernels.cu:303-305,
 //          kernels/attention/fused_attention.cu:671-676,
-//          kernels/attention/fused_attention_v4.cu:333-336.
+//          kernels/attention/fused_attention_v4.cu:333-336;
+// plus one additive schema with no counterpart in the reference,
+// fused_attention_gqa_varlen (per-sample lengths).
 
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
+
+#include <algorithm>
+#include <optional>
 
 #include "vlak_b200.h"
 
@@ -115,9 +120,111 @@ at::Tensor fused_attention_gqa_v4(const at::Tensor& q, const at::Tensor& k, cons
   return run_gqa(q, k, v, scale, prefix_len, dead_start, dead_end, true);
 }
 
+// kernels/attention/fused_attention.cu:525-598: (B, H, M, 64) layout, no GQA.
+// bf16 runs on the tensor cores (the reference's v2): analytic prefix mask
+// when prefix_len >= 0 (it wins over attn_mask, as there), else the bool
+// mask, else unmasked. fp32 / fp16 / fp64 run on the CUDA cores (v1), which
+// take no analytic mask.
+at::Tensor fused_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                           double scale, const std::optional<at::Tensor>& attn_mask,
+                           int64_t prefix_len) {
+  TORCH_CHECK(q_in.is_cuda() && q_in.dim() == 4, "expected 4D CUDA (B,H,M,D)");
+  TORCH_CHECK(q_in.size(3) == 64, "this kernel is specialized to head_dim 64");
+  TORCH_CHECK(k_in.dim() == 4 && v_in.dim() == 4 && k_in.size(3) == 64 && v_in.size(3) == 64,
+              "k/v head_dim 64");
+  TORCH_CHECK(k_in.size(2) == v_in.size(2), "k/v length mismatch");
+  TORCH_CHECK(k_in.size(0) == q_in.size(0) && k_in.size(1) == q_in.size(1) &&
+                  v_in.size(0) == q_in.size(0) && v_in.size(1) == q_in.size(1),
+              "k/v must be (B, H, N, 64) with the batch and heads of q");
+  TORCH_CHECK(k_in.device() == q_in.device() && v_in.device() == q_in.device(),
+              "q, k and v must be on the same CUDA device");
+  TORCH_CHECK(k_in.scalar_type() == q_in.scalar_type() && v_in.scalar_type() == q_in.scalar_type(),
+              "q, k and v must have the same dtype");
+  const int dt = dtype_code(q_in.scalar_type());
+  TORCH_CHECK(dt >= 0, "fused_attention: unsupported dtype ", q_in.scalar_type());
+  c10::cuda::CUDAGuard guard(q_in.device());
+  at::Tensor q = q_in.contiguous(), k = k_in.contiguous(), v = v_in.contiguous();
+  const int64_t B = q.size(0), H = q.size(1), M = q.size(2), N = k.size(2);
+  at::Tensor o = at::empty_like(q, at::MemoryFormat::Contiguous);
+  at::Tensor mask;
+  if (attn_mask.has_value()) {
+    mask = attn_mask->contiguous();
+    TORCH_CHECK(mask.scalar_type() == at::kBool, "attn_mask must be bool");
+    TORCH_CHECK(mask.dim() == 3 && mask.size(0) == B && mask.size(1) == M && mask.size(2) == N,
+                "attn_mask must be (B, M, N)");
+    TORCH_CHECK(mask.device() == q.device(), "attn_mask must be on the device of q");
+  }
+  if (B * H * M == 0) return o;
+  void* stream = c10::cuda::getCurrentCUDAStream().stream();
+  if (dt == VLAK_BF16) {
+    vlak_attn_gqa_args a{};
+    a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr();
+    a.B = B; a.M = M; a.N = N; a.H = H; a.Hkv = H;
+    // (B, H, seq, 64) seen as (B, seq, H, 64): strides of dims (b, seq, h)
+    const at::Tensor* ts[4] = {&q, &k, &v, &o};
+    int64_t* st[4] = {a.q_stride, a.k_stride, a.v_stride, a.o_stride};
+    for (int i = 0; i < 4; ++i) {
+      st[i][0] = ts[i]->stride(0);
+      st[i][1] = ts[i]->stride(2);
+      st[i][2] = ts[i]->stride(1);
+    }
+    a.scale = scale;
+    a.prefix_len = -1;
+    int status;
+    if (prefix_len >= 0) {
+      a.prefix_len = std::min(prefix_len, N);  // a prefix past N makes every key visible
+      status = vlak_attn_gqa_fwd(&a, stream);
+    } else if (mask.defined()) {
+      status = vlak_attn_gqa_masked_fwd(&a, mask.data_ptr(), M * N, N, stream);
+    } else {
+      status = vlak_attn_gqa_fwd(&a, stream);
+    }
+    check_status(status, "fused_attention launch failed");
+    return o;
+  }
+  TORCH_CHECK(prefix_len < 0, "analytic prefix mask requires the bf16 tensor-core path");
+  const int status = vlak_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dt, B,
+                                   H, M, N, mask.defined() ? mask.data_ptr() : nullptr, scale,
+                                   stream);
+  check_status(status, "fused_attention launch failed");
+  return o;
+}
+
+// Per-sample-length GQA attention (new schema; the reference leaves this
+// site, the C4 prefix attention, on SDPA with a materialised mask).
+at::Tensor fused_attention_gqa_varlen(const at::Tensor& q, const at::Tensor& k,
+                                      const at::Tensor& v, const at::Tensor& lengths_in,
+                                      double scale) {
+  vlak_attn_gqa_args a = gqa_args(q, k, v, scale, -1, 0, 0, "fused_attention_gqa_varlen");
+  TORCH_CHECK(lengths_in.is_cuda() && lengths_in.device() == q.device(),
+              "lengths must be on the device of q");
+  TORCH_CHECK(lengths_in.dim() == 1 && lengths_in.size(0) == a.B, "lengths must be (B,)");
+  TORCH_CHECK(lengths_in.scalar_type() == at::kInt || lengths_in.scalar_type() == at::kLong,
+              "lengths must be int32 or int64");
+  c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor lengths = lengths_in.contiguous();
+  check_status(vlak_attn_gqa_check(&a, nullptr, nullptr), "fused_attention_gqa_varlen");
+  at::Tensor o = at::empty({a.B, a.M, a.H, 64}, q.options());
+  a.o = o.data_ptr();
+  a.o_stride[0] = o.stride(0);
+  a.o_stride[1] = o.stride(1);
+  a.o_stride[2] = o.stride(2);
+  const int st = vlak_attn_gqa_varlen_fwd(
+      &a, lengths.data_ptr(), lengths.scalar_type() == at::kLong ? VLAK_I64 : VLAK_I32,
+      c10::cuda::getCurrentCUDAStream().stream());
+  check_status(st, "fused_attention_gqa_varlen launch failed");
+  return o;
+}
+
 }  // namespace
 
 TORCH_LIBRARY_FRAGMENT(vlak, m) {
+  m.def(
+      "fused_attention(Tensor q, Tensor k, Tensor v, float scale=-1., "
+      "Tensor? attn_mask=None, int prefix_len=-1) -> Tensor");
+  m.def(
+      "fused_attention_gqa_varlen(Tensor q, Tensor k, Tensor v, Tensor lengths, "
+      "float scale=-1.) -> Tensor");
   m.def("softmax(Tensor x, int version=4) -> Tensor");
   m.def(
       "fused_attention_gqa(Tensor q, Tensor k, Tensor v, float scale=-1., "
@@ -131,4 +238,6 @@ TORCH_LIBRARY_IMPL(vlak, CUDA, m) {
   m.impl("softmax", &softmax_lastdim);
   m.impl("fused_attention_gqa", &fused_attention_gqa);
   m.impl("fused_attention_gqa_v4", &fused_attention_gqa_v4);
+  m.impl("fused_attention", &fused_attention);
+  m.impl("fused_attention_gqa_varlen", &fused_attention_gqa_varlen);
 }
