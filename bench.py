@@ -281,6 +281,8 @@ def bench_ours(args, rank, world, local):
         line["cpu_baseline"] = cpu_baseline_sample(target_s=args.cpu_seconds)
     if rank == 0 and world == 1 and not args.no_softmax:
         line["softmax"] = bench_softmax()
+    if rank == 0 and world == 1 and not args.no_sites:
+        line["sites"] = bench_sites()
     return line
 
 
@@ -317,6 +319,80 @@ def bench_e2e(args, rank, world, shape, lo):
             "d2h_bytes_per_step": d2h,
             "note": "one call per step through torch.ops.vlak.fused_attention_gqa_v4 with "
                     "pinned host q/k/v copied in and o copied out inside the timed region"}
+
+
+def time_calls(fn, calls: int, warmup: int = 5) -> float:
+    """Mean seconds per call of fn() over `calls` back-to-back launches."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(calls):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / calls
+
+
+def bench_sites():
+    """Per-call times of the other attention sites on one GPU (reported, not
+    the headline): C3 expert self-attention at B = 1, 8, 64, C4 prefix
+    attention with per-sample lengths at B = 1, 16, 128, and the SigLIP
+    vision site (1, 12, 1024, 64) through vlak::fused_attention beside torch
+    SDPA. Inputs rotate over enough sets to exceed L2 where a call is small."""
+    import torch.nn.functional as F
+
+    from kernels.attention import (fused_attention, fused_attention_gqa_v4,
+                                   fused_attention_gqa_varlen)
+
+    peaks, _ = load_peaks()
+    res = {}
+    for B in (1, 8, 64):
+        s = wl.expert_shape(B)
+        nsets = max(1, min(64, (256 << 20) // wl.attn_bytes(s)))
+        sets = [wl.attn_inputs(s, seed=10 + i) for i in range(nsets)]
+        it = [0]
+
+        def call():
+            q, k, v = sets[it[0] % nsets]
+            it[0] += 1
+            fused_attention_gqa_v4(q, k, v, scale=0.125, prefix_len=s.P)
+
+        t = time_calls(call, 200)
+        res[f"C3_B{B}"] = {"us": round(t * 1e6, 2),
+                           "GB/s": round(wl.attn_bytes(s) / t / 1e9, 1),
+                           "TFLOP/s": round(wl.attn_flops(s) / t / 1e12, 2),
+                           "tensor_frac": round(wl.attn_flops(s) / t / 1e12 / peaks["bf16_tflops"], 4),
+                           "input_sets": nsets}
+        del sets
+    for B in (1, 16, 128):
+        s = wl.prefix_shape(B)
+        nsets = max(1, min(32, (256 << 20) // wl.attn_bytes(s)))
+        sets = [wl.attn_inputs(s, seed=20 + i) for i in range(nsets)]
+        L = wl.c4_lengths(B, seed=B)
+        it = [0]
+
+        def call():
+            q, k, v = sets[it[0] % nsets]
+            it[0] += 1
+            fused_attention_gqa_varlen(q, k, v, L)
+
+        t = time_calls(call, 100)
+        res[f"C4_varlen_B{B}"] = {"us": round(t * 1e6, 2),
+                                  "GB/s": round(wl.attn_bytes(s) / t / 1e9, 1),
+                                  "TFLOP/s": round(wl.varlen_flops(L) / t / 1e12, 2),
+                                  "input_sets": nsets}
+        del sets
+    q, k, v = wl.siglip_inputs()
+    flops = 4 * 64 * 12 * 1024 * 1024
+    t_ours = time_calls(lambda: fused_attention(q, k, v), 100)
+    t_sdpa = time_calls(lambda: F.scaled_dot_product_attention(q, k, v), 100)
+    res["SigLIP_1x12x1024"] = {"us": round(t_ours * 1e6, 2),
+                               "TFLOP/s": round(flops / t_ours / 1e12, 1),
+                               "torch_sdpa_us": round(t_sdpa * 1e6, 2)}
+    return res
 
 
 def bench_softmax():
@@ -446,6 +522,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-softmax", action="store_true")
+    ap.add_argument("--no-sites", action="store_true",
+                    help="skip the per-site attention timings (C3, C4, SigLIP)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--case", choices=["attn", "softmax"], default=None,
                     help="profiling mode: a few eager calls of one kernel, no JSON line")

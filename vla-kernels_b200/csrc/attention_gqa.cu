@@ -109,10 +109,14 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
 constexpr int kWaitMma = 1;      // MMA warp: P ready, K/V ready
 constexpr int kWaitSoftmax = 1;  // softmax warps: S ready
 
-constexpr int kThreads = 384;   // 3 warpgroups
-// control warps sit on SM sub-partitions 2 and 3: sub-partition 0 also hosts
-// the softmax warp of the second M-tile's first lane quarter
-constexpr int kWarpProducer = 10, kWarpMma = 11;
+// Two CTAs share each SM (each 10 warps, 256 TMEM columns, under 100 KB of
+// shared memory): the two CTAs' chunk pipelines are independent, so one
+// CTA's softmax warps compute while the other's wait on TMEM loads, barrier
+// hand-offs or the tensor pipe.
+constexpr int kThreads = 320;   // 10 warps
+constexpr int kCtasPerSm = 2;
+constexpr int kSoftmaxWarps = 8;  // 4 per M-tile, one per TMEM lane quarter
+constexpr int kWarpProducer = 8, kWarpMma = 9;
 // Key pairs whose exp2 runs on the FMA pipe instead of MUFU: bit (k % 8) of
 // the mask selects pair k of a 32-key group (full groups only).
 #ifndef VLAK_POLY_MASK
@@ -120,28 +124,29 @@ constexpr int kWarpProducer = 10, kWarpMma = 11;
 #endif
 constexpr uint32_t kPolyMask = VLAK_POLY_MASK;
 constexpr int kChunk = 64;      // keys per K/V chunk (S tile width)
-constexpr int kStages = 8;      // K/V ring depth (chunks)
+constexpr int kStages = 4;      // K/V ring depth (chunks) per CTA
 constexpr int kRowBytes = 128;  // 64 bf16 per row
 constexpr int kTileBytes = 128 * kRowBytes;        // one 128-row Q tile
 constexpr int kChunkBytes = kChunk * kRowBytes;    // one 64-key K (or V) chunk
-constexpr int kQBytes = 2 * 2 * kTileBytes;        // 2 buffers x 2 M-tiles
+constexpr int kQBytes = 2 * kTileBytes;            // the 2 M-tiles of one item
 constexpr int kKVBytes = kStages * kChunkBytes;    // K ring (V ring the same)
-constexpr int kOBytes = 2 * kTileBytes;            // output staging, one tile per M-tile
-constexpr int kSmemData = kQBytes + 2 * kKVBytes + kOBytes;  // 224 KB
-constexpr int kBarrierBytes = 512;
+constexpr int kSmemData = kQBytes + 2 * kKVBytes;  // 96 KB
+constexpr int kBarrierBytes = 256;
 constexpr int kSmemBytes = kSmemData + kBarrierBytes + 1024;  // + alignment slack
 
-// Tensor memory, per M-tile t (base 256 t): S double buffer [0,64) [64,128),
-// P double buffer [128,160) [160,192) (bf16 pairs), O [192,256).
-constexpr uint32_t kTileCols = 256, kColS = 0, kColP = 128, kColO = 192;
-constexpr uint32_t kTmemCols = 512;
+// Tensor memory (256 columns per CTA), per M-tile t at 128 t: S [0,64) and O
+// [64,128). P (bf16 pairs, two keys per 32-bit column) is written over the
+// first 32 columns of S, which the softmax has already read; the next chunk's
+// S is issued behind the P.V product that reads P (MMAs of one thread execute
+// in issue order).
+constexpr uint32_t kTileCols = 128, kColS = 0, kColO = 64;
+constexpr uint32_t kTmemCols = 256;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 struct __align__(64) Params {
   CUtensorMap tm_q;  // dims (64, H, M, B), box (64, G, MT, 1)
   CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 64, 1)
   CUtensorMap tm_v;
-  CUtensorMap tm_o;  // dims (64, H, M, B) of o, box (64, G, MT, 1): tile stores
   __nv_bfloat16* o;
   long long o_sb, o_sm, o_sh;  // element strides of o
   int B, M, N, H, Hkv, G;
@@ -168,13 +173,12 @@ struct __align__(64) Params {
 constexpr int kMaskAnalytic = 0, kMaskLength = 1, kMaskBool = 2;
 
 struct Barriers {
-  uint64_t q_full[2], q_empty[2];
+  uint64_t q_full, q_empty;
   uint64_t kv_full[kStages], kv_empty[kStages];
-  // S and P are double-buffered per tile; each buffer has its own pair of
-  // barriers, so no barrier ever runs two phases ahead of its waiter
-  uint64_t s_full[2][2];  // [tile][buffer]
-  uint64_t p_full[2];     // [buffer]: every softmax warp of the item's tiles arrives
-  uint64_t pv_done[2], o_full[2];
+  uint64_t s_full[2];   // [tile]: S of the chunk is in TMEM
+  uint64_t p_full[2];   // [tile]: the tile's 4 softmax warps wrote P
+  uint64_t pv_done[2];  // [tile]: P.V of the chunk completed
+  uint64_t o_full[2];   // [tile]: O of the item is final
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -251,16 +255,15 @@ __device__ __forceinline__ int chunk_cols(const Params& p, int c) {
 }
 
 template <int kMode>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gqa_attention_sm100(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte-swizzled operand tiles
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* q_smem = smem;                      // [2 buf][2 tile][128 x 128 B]
+  uint8_t* q_smem = smem;                      // [tile][128 x 128 B]
   uint8_t* k_smem = smem + kQBytes;            // [stage][64 x 128 B]
   uint8_t* v_smem = k_smem + kKVBytes;
-  uint8_t* o_smem = v_smem + kKVBytes;         // [tile][128 x 128 B], 128B-swizzled
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kSmemData);
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -268,11 +271,11 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->q_full[i], 1);
-      mbar_init(&bars->q_empty[i], 1);
-      for (int b = 0; b < 2; ++b) mbar_init(&bars->s_full[i][b], 1);
-      mbar_init(&bars->p_full[i], 8);  // one arrival per softmax warp of both tiles
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp of the tile
       mbar_init(&bars->pv_done[i], 1);
       mbar_init(&bars->o_full[i], 1);
     }
@@ -306,28 +309,29 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       prefetch_tmap(&p.tm_v);
-      prefetch_tmap(&p.tm_o);
     }
     __syncwarp();
-    uint32_t qi = 0, kv = 0;
-    // per full barrier: bit i of *_used = armed at least once, bit i of
-    // *_par = parity of its most recently armed phase (registers, no arrays)
-    uint32_t q_used = 0, q_par = 0, kv_used = 0, kv_par = 0;
+    uint32_t qi = 0, kv = 0, q_armed = 0;
+    // per K/V full barrier: bit i of kv_used = armed at least once, bit i of
+    // kv_par = parity of its most recently armed phase (registers, no arrays)
+    uint32_t kv_used = 0, kv_par = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
+    for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
       const Item it = decode_item<kMode>(p, item);
-      const int qs = qi & 1;
-      if (!__all_sync(kFullMask, bounded_wait(&bars->q_empty[qs], ((qi >> 1) & 1) ^ 1, abort_flag))) {
+      // an item with no live chunk is written as zeros by the softmax warps
+      // alone: no Q, no K/V, no barrier phase
+      if (next_live<kMode>(p, it, 0, n_chunks) < 0) continue;
+      // the single Q buffer is free once the previous item's S products completed
+      if (!__all_sync(kFullMask, bounded_wait(&bars->q_empty, (qi & 1) ^ 1, abort_flag))) {
         ok = false;
         break;
       }
       const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
-      mbar_arrive_expect_tx_elect(&bars->q_full[qs], qbytes);
-      q_par = (q_used & (1u << qs)) ? (q_par ^ (1u << qs)) : q_par;
-      q_used |= 1u << qs;
+      mbar_arrive_expect_tx_elect(&bars->q_full, qbytes);
+      ++q_armed;
       for (int t = 0; t < it.tiles_active; ++t)
-        tma_load_4d_elect(q_smem + (qs * 2 + t) * kTileBytes, &p.tm_q, &bars->q_full[qs], 0,
-                          it.kvh * p.G, it.m0 + t * p.MT, it.b);
+        tma_load_4d_elect(q_smem + t * kTileBytes, &p.tm_q, &bars->q_full, 0, it.kvh * p.G,
+                          it.m0 + t * p.MT, it.b);
       for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks)) {
         const int s = kv % kStages;
         if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
@@ -341,67 +345,57 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         tma_load_4d_elect(v_smem + s * kChunkBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
         ++kv;
       }
+      ++qi;
     }
     // never leave the CTA with copies in flight: wait for the last phase
     // armed on every full barrier (bounded, independent of the abort flag)
-    for (int i = 0; i < 2; ++i)
-      if (q_used & (1u << i)) bounded_wait(&bars->q_full[i], (q_par >> i) & 1u, abort_flag, false);
+    if (q_armed > 0) bounded_wait(&bars->q_full, (q_armed - 1) & 1, abort_flag, false);
     for (int s = 0; s < kStages; ++s)
       if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
     __syncwarp();
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
-    // Per item, chunk j of tile t:  S_t(j) -> buffer j%2 (issued two chunks
-    // ahead), then, once softmax has turned it into P_t(j) (buffer j%2),
-    // O_t (+)= P_t(j) V(j). Issue order per chunk: PV_t(j) then S_t(j+2), so
-    // the commit of S_t(j+2) also covers PV_t(j) (same thread, in order).
+    // Per item and chunk j of tile t: S_t(j) = Q_t K(j)^T into the tile's S
+    // columns; once softmax has written P_t(j) over them, O_t (+)= P_t(j) V(j)
+    // and, right behind it in issue order, S_t(j+1) over the same columns.
     // The whole warp runs the loop (converged); one elected lane issues.
     {
-      uint32_t qi = 0, kv = 0, pph = 0;  // bit b: parity expected on p_full[b]
+      uint32_t qi = 0, kv = 0;
+      uint32_t pph = 0;  // bit t: parity expected on p_full[t]
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x, ++qi) {
+      for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
         const Item it = decode_item<kMode>(p, item);
-        const int qs = qi & 1;
-        if (!__all_sync(kFullMask, bounded_wait(&bars->q_full[qs], (qi >> 1) & 1, abort_flag))) {
+        const bool two = it.tiles_active == 2;
+        if (next_live<kMode>(p, it, 0, n_chunks) < 0) continue;  // zeros, written by softmax
+        if (!__all_sync(kFullMask, bounded_wait(&bars->q_full, qi & 1, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t q_base = smem_u32(q_smem + qs * 2 * kTileBytes);
-        // Each burst below is straight-line code: both tiles and all K-steps
-        // unrolled, absent ones predicated off inside the issuing asm.
-        const uint32_t two = it.tiles_active == 2 ? 1u : 0u;
-        auto issue_s = [&](int c, int j, uint32_t en) {  // S_t(j) for every active tile
+        const uint32_t q_base = smem_u32(q_smem);
+        auto issue_s = [&](int t, int c, int j) {  // four K16 steps, 32 B apart in a swizzled row
           const int s = (kv + j) % kStages;
           const uint32_t idesc = idesc_bf16_f32(128, chunk_cols(p, c), false);
+          const uint32_t a0 = q_base + t * kTileBytes;
           const uint32_t b0 = smem_u32(k_smem + s * kChunkBytes);
+          const uint32_t d = tmem + t * kTileCols + kColS;
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const uint32_t on = (t == 0 ? 1u : two) & en;
-            const uint32_t a0 = q_base + t * kTileBytes;
-            const uint32_t d = tmem + t * kTileCols + kColS + (j & 1) * kChunk;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)  // head_dim 64 = 4 x K16, 32 B apart in a swizzled row
-              umma_ss_elect(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0, on);
-            umma_commit_elect(&bars->s_full[t][j & 1], on);
-          }
+          for (int k = 0; k < 4; ++k)
+            umma_ss_elect(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, k > 0);
+          umma_commit_elect(&bars->s_full[t]);
         };
-        auto issue_pv = [&](int c, int j) {  // O_t (+)= P_t(j) V(j) for every active tile
+        auto issue_pv = [&](int t, int c, int j) {  // 16 keys = 8 packed columns of P, 2 KB of V
           const int s = (kv + j) % kStages;
-          const int nk = chunk_cols(p, c) / 16;  // 16 keys = 8 packed columns of P, 2 KB of V
+          const int nk = chunk_cols(p, c) / 16;
           const uint32_t idesc = idesc_bf16_f32(128, 64, true);
           const uint32_t b0 = smem_u32(v_smem + s * kChunkBytes);
+          const uint32_t a = tmem + t * kTileCols + kColS;
+          const uint32_t d = tmem + t * kTileCols + kColO;
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const uint32_t on = t == 0 ? 1u : two;
-            const uint32_t a = tmem + t * kTileCols + kColP + (j & 1) * (kChunk / 2);
-            const uint32_t d = tmem + t * kTileCols + kColO;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              umma_ts_elect(d, a + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc, (j > 0 || k > 0) ? 1u : 0u,
-                            (k < nk) ? on : 0u);
-            umma_commit_elect(&bars->pv_done[t], on);
-          }
+          for (int k = 0; k < 4; ++k)
+            umma_ts_elect(d, a + 8 * k, sdesc_sw128(b0 + 2048 * k), idesc,
+                          (j > 0 || k > 0) ? 1u : 0u, k < nk ? 1u : 0u);
+          umma_commit_elect(&bars->pv_done[t]);
         };
         auto wait_kv = [&](int j) {
           const uint32_t n = kv + j;
@@ -410,59 +404,69 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           tc_fence_after();
           return true;
         };
-        auto wait_p = [&](int j) {
-          const uint32_t bit = 1u << (j & 1);
-          if (!__all_sync(kFullMask, bounded_wait<kWaitMma>(&bars->p_full[j & 1], (pph & bit) ? 1u : 0u, abort_flag)))
+        auto wait_p = [&](int t) {
+          const uint32_t bit = 1u << t;
+          if (!__all_sync(kFullMask, bounded_wait<kWaitMma>(&bars->p_full[t], (pph & bit) ? 1u : 0u, abort_flag)))
             return false;
           pph ^= bit;
           tc_fence_after();
           return true;
         };
         int cur = next_live<kMode>(p, it, 0, n_chunks);
-        int nxt = cur >= 0 ? next_live<kMode>(p, it, cur + 1, n_chunks) : -1;
         int j = 0;
-        if (cur >= 0) {
-          if (!wait_kv(0)) { ok = false; break; }
-          issue_s(cur, 0, 1u);
-        }
-        if (nxt >= 0) {
-          if (!wait_kv(1)) { ok = false; break; }
-          issue_s(nxt, 1, 1u);
-        }
+        // S of chunk 0 is issued after the previous item's last P.V, which
+        // read P from the same columns; tcgen05.mma operations of one thread
+        // execute in issue order, so no completion wait is needed in between.
+        if (!wait_kv(0)) { ok = false; break; }
+        issue_s(0, cur, 0);
+        if (two) issue_s(1, cur, 0);
         while (cur >= 0) {
-          const int nn = nxt >= 0 ? next_live<kMode>(p, it, nxt + 1, n_chunks) : -1;  // chunk j+2
-          // both waits first (both tiles' P, the K/V two chunks ahead), then
-          // one branch-free burst: PV of every tile, then the S two chunks ahead
-          if (!wait_p(j)) { ok = false; break; }
-          if (nn >= 0 && !wait_kv(j + 2)) { ok = false; break; }
-          const int cs = nn >= 0 ? nn : cur;  // any valid chunk when S is off
-          issue_pv(cur, j);
-          issue_s(cs, j + 2, nn >= 0 ? 1u : 0u);
-          umma_commit_elect(&bars->kv_empty[(kv + j) % kStages]);
+          const int nxt = next_live<kMode>(p, it, cur + 1, n_chunks);
+          if (nxt < 0) umma_commit_elect(&bars->q_empty);  // the item's last S products read Q
+          // per tile: P of chunk j ready -> O += P V(j), then S of chunk j+1
+          // over the S/P columns (in issue order after the product reading P)
+          if (!wait_p(0)) { ok = false; break; }
+          issue_pv(0, cur, j);
+          if (nxt >= 0) {
+            if (!wait_kv(j + 1)) { ok = false; break; }
+            issue_s(0, nxt, j + 1);
+          }
+          if (two) {
+            if (!wait_p(1)) { ok = false; break; }
+            issue_pv(1, cur, j);
+            if (nxt >= 0) issue_s(1, nxt, j + 1);
+          }
+          umma_commit_elect(&bars->kv_empty[(kv + j) % kStages]);  // K and V of chunk j read
           cur = nxt;
-          nxt = nn;
           ++j;
         }
         if (!ok) break;
+        // one o_full phase per item with live chunks; each follows the
+        // softmax warps' arrivals on p_full, so no phase can run ahead of them
         umma_commit_elect(&bars->o_full[0]);
-        umma_commit_elect(&bars->o_full[1], two);
-        umma_commit_elect(&bars->q_empty[qs]);
+        umma_commit_elect(&bars->o_full[1], two ? 1u : 0u);
         kv += j;
+        ++qi;
       }
       // every issued MMA must complete before TMEM is released
       umma_commit_elect(&bars->drain);
       bounded_wait(&bars->drain, 0, abort_flag, false);
     }
     __syncwarp();  // reconverge before the CTA-wide barrier and the dealloc
-  } else if (warp < 8) {
+  } else if (warp < kSoftmaxWarps) {
     // ------------------------------------------------------------ softmax
-    const int t = warp >> 2;                // M-tile of this group
-    const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+    // Warp w owns TMEM lane quarter w % 4 (32 query rows) of M-tile w / 4.
+    // A chunk's 64 keys are handled as two 32-key groups: load, max, exp,
+    // P store per group, so a thread holds 32 scores at a time.
+    const int t = warp >> 2;
+    const int quarter = warp & 3;
     const int row = quarter * 32 + lane;    // TMEM lane = row within the tile
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + t * kTileCols;
+    const uint32_t tS = tbase + kColS;      // S; P (bf16 pairs) over its first 32 columns
     const uint32_t tO = tbase + kColO;
     const int m_local = row / p.G;
-    uint32_t sph = 0, oph = 0, pv_seen = 0;  // sph bit b: parity on s_full[t][b]; pv_seen: P.V products so far
+    const int g = row - m_local * p.G;
+    uint32_t sph = 0, oph = 0, pv_seen = 0;  // pv_seen: this tile's P.V products so far
     bool ok = true;
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
@@ -483,111 +487,105 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       const uint8_t* mrow = nullptr;
       if (kMode == kMaskBool && valid)
         mrow = p.mask + static_cast<long long>(it.b) * p.mask_sb + static_cast<long long>(m) * p.mask_sm;
+      __nv_bfloat16* orow = p.o + static_cast<long long>(it.b) * p.o_sb +
+                            static_cast<long long>(m) * p.o_sm +
+                            static_cast<long long>(it.kvh * p.G + g) * p.o_sh;
+      if (next_live<kMode>(p, it, 0, n_chunks) < 0) {
+        // no key visible to any row of the item: zeros, no barrier phase
+        if (valid) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v) reinterpret_cast<uint4*>(orow)[v] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
       for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks), ++j) {
         // warp-uniform outcome: the TMEM accesses below are warp-collective
-        if (!__all_sync(kFullMask, bounded_wait<kWaitSoftmax>(&bars->s_full[t][j & 1], (sph >> (j & 1)) & 1u, abort_flag))) {
+        if (!__all_sync(kFullMask, bounded_wait<kWaitSoftmax>(&bars->s_full[t], sph, abort_flag))) {
           ok = false;
           break;
         }
-        sph ^= 1u << (j & 1);
+        sph ^= 1u;
         tc_fence_after();
         if (warp_active) {
           const int c0 = c * kChunk;
           const int ncols = chunk_cols(p, c);
-          const uint32_t tS = tbase + kColS + (j & 1) * kChunk;
-          const uint32_t tP = tbase + kColP + (j & 1) * (kChunk / 2);
-          // S of this chunk in one batch and one wait; columns past the chunk
-          // width fail the visibility test (they lie at or past N >= e2). The
-          // mask is applied where a value is used; S is never rewritten.
-          float sv[kChunk / 32][32];
-#pragma unroll
-          for (int gq = 0; gq < kChunk / 32; ++gq) tmem_ld32(tS + 32 * gq, sv[gq]);
-          // Warp-uniform class of each 32-key group: every valid row of the
-          // warp sees all 32 keys (no mask arithmetic) or none of them (no
-          // exp); otherwise each row's visible keys as a bit mask. Rows past
-          // the tile or past M do not vote (their outputs are discarded), so
-          // the analytic and the bool-mask form of one mask classify alike.
-          uint32_t vmask[kChunk / 32];
-          uint32_t full_bits = 0, none_bits = 0;
+          float alpha_o = 1.f, alpha_p = 1.f;  // this chunk's rescale factors (O, first group's P)
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             const int g0 = c0 + 32 * gq;
             const bool in_chunk = 32 * gq < ncols;
+            // Warp-uniform class of the 32-key group: every valid row of the
+            // warp sees all 32 keys (no mask arithmetic) or none of them (no
+            // exp); otherwise each row's visible keys as a bit mask. Rows past
+            // the tile or past M do not vote (their outputs are discarded), so
+            // the analytic and the bool-mask form of one mask classify alike.
             auto low = [](int n) -> uint32_t {
               return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
             };
-            bool full, none;
+            bool full_l, none_l;
             uint32_t vm = 0u;
             if (kMode == kMaskBool) {
               if (in_chunk && mrow != nullptr) vm = mask_bits32(p, mrow, g0);
-              full = !valid || (in_chunk && vm == 0xffffffffu);
-              none = !valid || vm == 0u;
+              full_l = !valid || (in_chunk && vm == 0xffffffffu);
+              none_l = !valid || vm == 0u;
             } else {
-              full = !valid || (in_chunk && ((g0 + 32 <= rds) || (g0 >= rde && g0 + 32 <= e2)));
-              none = !valid || !in_chunk || ((g0 >= rds) && (g0 + 32 <= rde || g0 >= e2));
+              full_l = !valid || (in_chunk && ((g0 + 32 <= rds) || (g0 >= rde && g0 + 32 <= e2)));
+              none_l = !valid || !in_chunk || ((g0 >= rds) && (g0 + 32 <= rde || g0 >= e2));
             }
-            full_bits |= (__all_sync(kFullMask, full) ? 1u : 0u) << gq;
-            none_bits |= (__all_sync(kFullMask, none) ? 1u : 0u) << gq;
-            if (kMode != kMaskBool && !(((full_bits | none_bits) >> gq) & 1u))
+            const bool full = __all_sync(kFullMask, full_l);
+            const bool none = __all_sync(kFullMask, none_l);
+            if (kMode != kMaskBool && !full && !none)
               vm = valid ? (low(rds - g0) | (low(e2 - g0) & ~low(rde - g0))) : 0u;
-            vmask[gq] = vm;
-          }
-          tmem_wait_ld();
-          // row max with four independent accumulators (short dependency chains)
-          float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            float sv[32];
+            float mx = -INFINITY;
+            if (!none) {
+              tmem_ld32(tS + 32 * gq, sv);
+              tmem_wait_ld();
+              // group max with four independent accumulators
+              float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+              if (full) {
 #pragma unroll
-          for (int gq = 0; gq < kChunk / 32; ++gq) {
-            if ((none_bits >> gq) & 1u) continue;
-            if ((full_bits >> gq) & 1u) {
+                for (int i = 0; i < 32; i += 2)
+                  mxa[(i >> 1) & 3] = fmax3(mxa[(i >> 1) & 3], sv[i], sv[i + 1]);
+              } else {
 #pragma unroll
-              for (int i = 0; i < 32; i += 2)
-                mxa[(i >> 1) & 3] = fmax3(mxa[(i >> 1) & 3], sv[gq][i], sv[gq][i + 1]);
-            } else {
-              const uint32_t vm = vmask[gq];
-#pragma unroll
-              for (int i = 0; i < 32; i += 2)
-                mxa[(i >> 1) & 3] = fmax3(mxa[(i >> 1) & 3],
-                                          ((vm >> i) & 1u) ? sv[gq][i] : -INFINITY,
-                                          ((vm >> (i + 1)) & 1u) ? sv[gq][i + 1] : -INFINITY);
+                for (int i = 0; i < 32; i += 2)
+                  mxa[(i >> 1) & 3] = fmax3(mxa[(i >> 1) & 3], ((vm >> i) & 1u) ? sv[i] : -INFINITY,
+                                            ((vm >> (i + 1)) & 1u) ? sv[i + 1] : -INFINITY);
+              }
+              mx = fmax3(fmaxf(mxa[0], mxa[1]), mxa[2], mxa[3]);
             }
-          }
-          const float mx = fmax3(fmaxf(mxa[0], mxa[1]), mxa[2], mxa[3]);
-          const float mz = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
-          // The reference max moves only when this chunk's max exceeds it by
-          // more than the threshold; O and l are then rescaled by alpha (after
-          // P is written, so S is no longer live).
-          bool need = false;
-          float alpha = 1.f;
-          if (j == 0) {
-            m_run = mz;
-          } else {
-            need = mz > m_run + kRescaleThreshold;
-            if (need) {
+            const float mz = mx * p.scale_log2;  // -inf stays -inf (scale > 0)
+            // The reference max moves only when a group's max exceeds it by
+            // more than the threshold; O, l and the P already written for this
+            // chunk are then rescaled by alpha (below, once the scores are dead).
+            float alpha = 1.f;
+            if (j == 0 && gq == 0) {
+              m_run = mz;
+            } else if (mz > m_run + kRescaleThreshold) {
               alpha = ex2(m_run - mz);
               m_run = mz;
             }
-          }
-          // P = exp2(s * scale_log2 - mref) as bf16 pairs into TMEM. Key pairs
-          // go through the f32x2 FMA pipe; exps run on MUFU except for the pairs
-          // kPolyMask selects, which use the FMA-pipe polynomial (full groups
-          // only, where no -inf occurs).
-          const float nref = (m_run == -INFINITY) ? 0.f : -m_run;
-          const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2);
-          const uint64_t nr2 = f2_pack(nref, nref);
-          uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // four (+0.f, +0.f) pairs
-#pragma unroll
-          for (int gq = 0; gq < kChunk / 32; ++gq) {
-            if (32 * gq >= ncols) continue;
+            if (!in_chunk) continue;  // (no keys: alpha is 1)
+            // P = exp2(s * scale_log2 - mref) as bf16 pairs over the group's
+            // first 16 columns of S. Key pairs go through the f32x2 FMA pipe;
+            // exps run on MUFU except for the pairs kPolyMask selects, which
+            // use the FMA-pipe polynomial (full groups only, where no -inf
+            // occurs).
+            const float nref = (m_run == -INFINITY) ? 0.f : -m_run;
+            const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2);
+            const uint64_t nr2 = f2_pack(nref, nref);
+            uint64_t acc[2] = {0ull, 0ull};  // two (+0.f, +0.f) pairs
             uint32_t pk[16];
-            if ((none_bits >> gq) & 1u) {
+            if (none) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) pk[i] = 0u;
-            } else if ((full_bits >> gq) & 1u) {
+            } else if (full) {
 #pragma unroll
               for (int k = 0; k < 16; ++k) {
-                const uint64_t x = f2_fma(f2_pack(sv[gq][2 * k], sv[gq][2 * k + 1]), sl2, nr2);
+                const uint64_t x = f2_fma(f2_pack(sv[2 * k], sv[2 * k + 1]), sl2, nr2);
                 uint64_t e;
                 float x0, x1;
                 f2_unpack(x, x0, x1);
@@ -596,101 +594,104 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
                 } else {
                   e = f2_pack(ex2(x0), ex2(x1));
                 }
-                acc[k & 3] = f2_add(acc[k & 3], e);
+                acc[k & 1] = f2_add(acc[k & 1], e);
                 float e0, e1;
                 f2_unpack(e, e0, e1);
                 pk[k] = pack_bf16x2(e0, e1);
               }
             } else {
-              const uint32_t vm = vmask[gq];
 #pragma unroll
               for (int k = 0; k < 16; ++k) {
-                const uint64_t x = f2_fma(f2_pack(sv[gq][2 * k], sv[gq][2 * k + 1]), sl2, nr2);
+                const uint64_t x = f2_fma(f2_pack(sv[2 * k], sv[2 * k + 1]), sl2, nr2);
                 float x0, x1;
                 f2_unpack(x, x0, x1);
                 const float e0 = ((vm >> (2 * k)) & 1u) ? ex2(x0) : 0.f;
                 const float e1 = ((vm >> (2 * k + 1)) & 1u) ? ex2(x1) : 0.f;
-                acc[k & 3] = f2_add(acc[k & 3], f2_pack(e0, e1));
+                acc[k & 1] = f2_add(acc[k & 1], f2_pack(e0, e1));
                 pk[k] = pack_bf16x2(e0, e1);
               }
             }
-            tmem_st16(tP + 16 * gq, pk);
+            tmem_st16(tS + 16 * gq, pk);
+            float acc0, acc1;
+            f2_unpack(f2_add(acc[0], acc[1]), acc0, acc1);
+            l_run = l_run * alpha + (acc0 + acc1);
+            alpha_o *= alpha;
+            if (gq > 0) alpha_p = alpha;
           }
-          float acc0, acc1;
-          f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), acc0, acc1);
-          const float lsum = acc0 + acc1;
-          l_run = l_run * alpha + lsum;
-          tmem_wait_st();
-          if (__any_sync(kFullMask, need)) {
-            // O_t must hold the previous P.V of this tile before it is scaled
-            if (!__all_sync(kFullMask, bounded_wait(&bars->pv_done[t], (pv_seen - 1) & 1, abort_flag))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              float o[32];
-              tmem_ld32(tO + 32 * half, o);
+          // Rare: the reference max moved within the chunk. O (P.V of chunks
+          // 0 .. j-1) is rescaled by the product of the chunk's factors and
+          // the first group's P by the second group's factor; the scores are
+          // no longer live here.
+          if (__any_sync(kFullMask, alpha_o != 1.f)) {
+            if (__any_sync(kFullMask, alpha_p != 1.f)) {
+              tmem_wait_st();  // the first group's P store has landed
+              float pf[16];
+              tmem_ld16(tS, pf);
               tmem_wait_ld();
+              uint32_t pw[16];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= alpha;
-              tmem_st32f(tO + 32 * half, o);
+              for (int i = 0; i < 16; ++i) {
+                const uint32_t w = __float_as_uint(pf[i]);
+                pw[i] = pack_bf16x2(__uint_as_float(w << 16) * alpha_p,
+                                    __uint_as_float(w & 0xffff0000u) * alpha_p);
+              }
+              tmem_st16(tS, pw);
             }
-            tmem_wait_st();
+            if (j > 0) {
+              if (!__all_sync(kFullMask, bounded_wait(&bars->pv_done[t], (pv_seen - 1) & 1, abort_flag))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+#pragma unroll 1
+              for (int q4 = 0; q4 < 4; ++q4) {  // 16 columns at a time keeps the registers low
+                float o[16];
+                tmem_ld16(tO + 16 * q4, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] *= alpha_o;
+                tmem_st16f(tO + 16 * q4, o);
+              }
+            }
           }
+          tmem_wait_st();
         }
         ++pv_seen;
         tc_fence_before();
-        // eight arrivals complete a phase; with one active tile its warps
-        // arrive for the absent ones too
-        mbar_arrive_elect(&bars->p_full[j & 1], it.tiles_active == 2 ? 1u : 2u);
+        mbar_arrive_elect(&bars->p_full[t], 1u);
       }
       if (!ok) break;
-      // epilogue: O / l -> bf16 rows, staged in shared memory (128B-swizzled,
-      // the layout of the output tensor map) and written by one TMA store
+      // epilogue: O / l -> bf16 rows, written from registers (each thread one
+      // 128-byte row of o)
       if (!__all_sync(kFullMask, bounded_wait(&bars->o_full[t], oph, abort_flag))) { ok = false; break; }
       oph ^= 1;
       tc_fence_after();
-      uint8_t* stage = o_smem + t * kTileBytes;
-      const bool leader = (quarter == 0 && lane == 0);
-      // the previous store from this staging tile must have read it
-      if (leader) bulk_wait_read0();
-      named_barrier(1 + t, 128);
       if (warp_active) {
         const bool any = (j > 0) && (l_run > 0.f);
         const float inv = any ? 1.f / l_run : 0.f;
-        uint8_t* srow = stage + row * kRowBytes;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {  // 32 columns of O at a time
-          float o[32];
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {  // 16 columns of O at a time
+          float o[16];
           if (j > 0) {
-            tmem_ld32(tO + 32 * half, o);
+            tmem_ld16(tO + 16 * q4, o);
             tmem_wait_ld();
           }
           if (valid) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
+            for (int v = 0; v < 2; ++v) {
               uint32_t w[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e)
                 w[e] = any ? pack_bf16x2(o[v * 8 + 2 * e] * inv, o[v * 8 + 2 * e + 1] * inv) : 0u;
-              const int cv = half * 4 + v;  // 16-byte chunk of the 128-byte row
-              *reinterpret_cast<uint4*>(srow + ((cv ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(orow + q4 * 16 + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
             }
           }
         }
       }
-      fence_proxy_async_smem();
+      // the next item's first P.V overwrites O once this tile's softmax warps
+      // arrive on p_full, after these loads
       tc_fence_before();
-      named_barrier(1 + t, 128);
-      if (leader) {
-        tma_store_4d(&p.tm_o, stage, 0, it.kvh * p.G, m_first, it.b);
-        bulk_commit_group();
-      }
     }
-    // stores must finish reading shared memory before the CTA exits
-    if (quarter == 0 && lane == 0) bulk_wait_all0();
   }
 
   tc_fence_before();
@@ -890,12 +891,9 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
   st = encode_map(&prm.tm_v, a->v, a->Hkv, a->N, a->B, a->v_stride[2], a->v_stride[1],
                   a->v_stride[0], 1, kChunk, "v");
   if (st != VLAK_OK) return st;
-  st = encode_map(&prm.tm_o, a->o, a->H, a->M, a->B, a->o_stride[2], a->o_stride[1],
-                  a->o_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "o");
-  if (st != VLAK_OK) return st;
 
   if (dev.device >= 64) return set_error(VLAK_ERR_CUDA, "device ordinal out of range");
-  const int grid = static_cast<int>(std::min<long long>(items, dev.sm_count));
+  const int grid = static_cast<int>(std::min<long long>(items, static_cast<long long>(dev.sm_count) * kCtasPerSm));
   cudaError_t e = ms.mode == kMaskLength ? launch_mode<kMaskLength>(prm, grid, cs, dev.device)
                   : ms.mode == kMaskBool ? launch_mode<kMaskBool>(prm, grid, cs, dev.device)
                                          : launch_mode<kMaskAnalytic>(prm, grid, cs, dev.device);

@@ -441,6 +441,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&u)[16
         "r"(u[14]), "r"(u[15])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "f"(r[0]), "f"(r[1]), "f"(r[2]), "f"(r[3]), "f"(r[4]), "f"(r[5]), "f"(r[6]),
+        "f"(r[7]), "f"(r[8]), "f"(r[9]), "f"(r[10]), "f"(r[11]), "f"(r[12]), "f"(r[13]),
+        "f"(r[14]), "f"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st32f(uint32_t taddr, const float (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"

@@ -96,3 +96,28 @@ def attn_flops(s: AttnShape) -> int:
 def attn_bytes(s: AttnShape) -> int:
     """Algorithmic HBM bytes: read q, k, v once and write o once (bf16)."""
     return 2 * HEAD_DIM * s.B * (2 * s.M * s.H + 2 * s.N * s.Hkv)
+
+
+# C4: SmolVLA VLM-prefix attention, bidirectional over per-sample lengths
+# L_b ~ U{150..241} (seeded); the compacted variant is M = N = 197, all visible.
+def prefix_shape(B: int, seq: int = 241) -> AttnShape:
+    return AttnShape(B=B, M=seq, N=seq, H=15, Hkv=5, P=seq)
+
+
+def c4_lengths(B: int, device="cuda", seed: int = 0, lo: int = 150, hi: int = 241) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(lo, hi + 1, (B,), generator=g).to(device)
+
+
+def varlen_flops(lengths, H: int = 15) -> int:
+    """Algorithmic FLOPs of per-sample-length attention: L_b^2 visible pairs
+    per (b, h)."""
+    L = torch.as_tensor(lengths).to(torch.int64).cpu()
+    return int(4 * HEAD_DIM * H * (L * L).sum().item())
+
+
+# SigLIP vision attention site: (1, 12, 1024, 64) bf16, unmasked (B, H, M, 64)
+def siglip_inputs(B: int = 1, H: int = 12, M: int = 1024, device="cuda", seed: int = 0):
+    g = _gen(device, seed)
+    mk = lambda: torch.randn(B, H, M, HEAD_DIM, device=device, generator=g).to(torch.bfloat16)  # noqa: E731
+    return mk(), mk(), mk()
