@@ -395,34 +395,61 @@ def bench_sites():
     return res
 
 
-def bench_softmax():
-    """C2 wide-row bf16 softmax (8192 x 32768) and C1 fp32, 1 GPU, cold inputs."""
+def time_softmax_flushed(x, iters: int = 10) -> float:
+    """Median seconds of softmax(x, "auto") with L2 flushed before every call:
+    a 256 MB write (larger than the 126 MB L2), then a 256 MB read of another
+    buffer, so the timed kernel starts with a cold L2 that holds no dirty lines
+    (their write-back would otherwise be charged to it)."""
     from kernels.softmax import softmax
+
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
+    clean = torch.ones(64 * 2**20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        softmax(x, "auto")
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        torch.sum(clean, dim=0, out=sink)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        softmax(x, "auto")
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / 1e3)
+    del flush, clean
+    return statistics.median(times)
+
+
+def bench_softmax():
+    """C2 bf16 softmax over its whole grid (rows {256, 1024, 8192} x cols {241,
+    1024, 4096, 16384, 32768} and the narrow [983040, 291]) and C1 fp32
+    [4096, 1024], 1 GPU, L2 flushed before every call. The 8192 x 32768 line
+    is the headline; cases below ~1 MB are launch-bound and reported only."""
+    from kernels.softmax import _auto_version
 
     peaks, _ = load_peaks()
     res = {}
-    for name, x in (("C2_bf16_8192x32768", wl.softmax_c2(8192, 32768)),
-                    ("C1_fp32_4096x1024", wl.softmax_c1())):
-        xs = [x] + ([x.clone() for _ in range(3)] if x.numel() * x.element_size() < 2**28 else [])
-        flush = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
-        for _ in range(3):
-            softmax(xs[0], "auto")
-        times = []
-        for i in range(10):
-            flush.zero_()  # evict L2 (256 MB > 126 MB)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            softmax(xs[i % len(xs)], "auto")
-            e1.record()
-            torch.cuda.synchronize()
-            times.append(e0.elapsed_time(e1) / 1e3)
-        t = statistics.median(times)
+
+    def one(name, x):
+        t = time_softmax_flushed(x)
         nbytes = wl.softmax_bytes(x.shape[0], x.shape[1], x.element_size())
         gbs = nbytes / t / 1e9
         res[name] = {"us": round(t * 1e6, 2), "GB/s": round(gbs, 1),
-                     "frac_hbm": round(gbs / peaks["hbm_gbs"], 4), "l2": "flushed"}
-        del xs, flush
+                     "frac_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                     "l2": "flushed (256 MB write, then 256 MB clean read)",
+                     "version": _auto_version(x)}
+
+    one("C2_bf16_8192x32768", wl.softmax_c2(8192, 32768))
+    one("C1_fp32_4096x1024", wl.softmax_c1())
+    grid = {}
+    for rows in wl.C2_ROWS:
+        for cols in wl.C2_COLS:
+            if (rows, cols) == (8192, 32768):
+                continue
+            one(f"C2_{rows}x{cols}", wl.softmax_c2(rows, cols))
+    one(f"C2_narrow_{wl.C2_NARROW[0]}x{wl.C2_NARROW[1]}", wl.softmax_c2(*wl.C2_NARROW))
     return res
 
 

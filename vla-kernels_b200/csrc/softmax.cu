@@ -76,6 +76,22 @@ struct WarpGroup {
   __device__ __forceinline__ float max(float v) const { return warp_max(v); }
   __device__ __forceinline__ float sum(float v) const { return warp_sum(v); }
 };
+// LPR consecutive lanes of a warp (LPR = 8 or 16): shuffles stay inside the
+// lane group and name only its lanes, so a group whose row lies past the end
+// of the tensor may return early.
+template <int LPR> struct SubWarpGroup {
+  unsigned mask;
+  __device__ __forceinline__ float max(float v) const {
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(mask, v, o));
+    return v;
+  }
+  __device__ __forceinline__ float sum(float v) const {
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(mask, v, o);
+    return v;
+  }
+};
 // Whole block; two separate slots so max and sum need one barrier each.
 template <int NT> struct BlockGroup {
   float* smax;
@@ -369,6 +385,31 @@ __global__ void __launch_bounds__(256) softmax_warp_reg(const T* __restrict__ x,
   row_softmax_reg<T, RV, 32>(x + row * cols, y + row * cols, cols, threadIdx.x & 31, WarpGroup{});
 }
 
+// The same for narrow rows with LPR (8 or 16) lanes per row: a warp owns
+// 32 / LPR rows, and a row's vectors fill its lanes' RV slots far better than
+// a whole warp would (a 291-column bf16 row is about 37 vectors: 40 slots at
+// LPR 8 against 64 at LPR 32), which the narrow, issue-bound case needs.
+template <typename T, int RV, int LPR>
+__global__ void __launch_bounds__(256) softmax_subwarp_reg(const T* __restrict__ x,
+                                                           T* __restrict__ y, int64_t rows,
+                                                           int cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) *
+                          (32 / LPR) + lane / LPR;
+  if (row >= rows) return;
+  const unsigned mask = ((1u << LPR) - 1u) << (lane & ~(LPR - 1));
+  row_softmax_reg<T, RV, LPR>(x + row * cols, y + row * cols, cols, lane & (LPR - 1),
+                              SubWarpGroup<LPR>{mask});
+}
+
+template <typename T, int RV, int LPR>
+cudaError_t launch_subwarp(const T* x, T* y, int64_t rows, int cols, cudaStream_t st) {
+  const int64_t per_block = 8 * (32 / LPR);
+  const int64_t blocks = (rows + per_block - 1) / per_block;
+  softmax_subwarp_reg<T, RV, LPR><<<static_cast<unsigned>(blocks), 256, 0, st>>>(x, y, rows, cols);
+  return cudaGetLastError();
+}
+
 // v1 for rows wider than a warp's registers: online pass + write pass
 template <typename T, bool kVector>
 __global__ void __launch_bounds__(256) softmax_warp_stream(const T* __restrict__ x,
@@ -503,6 +544,17 @@ cudaError_t dispatch(const T* x, T* y, int64_t rows, int cols, int version, cuda
   const int nvec = cols / V;
   // largest body a warp keeps in registers: 8 vectors per lane
   const int warp_rv = nvec <= 32 ? 1 : nvec <= 64 ? 2 : nvec <= 128 ? 4 : nvec <= 256 ? 8 : 0;
+  // Narrow rows (versions 1 and 4): a lane group of 8 or 16 per row with as
+  // many vector slots as the row needs (the +1 covers a row whose head and
+  // tail make one more partial vector).
+  if (version == 1 || (version != 2 && version != 3 && nvec <= 128)) {
+    const int need = nvec + 1;
+    if (need <= 16) return launch_subwarp<T, 2, 8>(x, y, rows, cols, st);
+    if (need <= 32) return launch_subwarp<T, 4, 8>(x, y, rows, cols, st);
+    if (need <= 40) return launch_subwarp<T, 5, 8>(x, y, rows, cols, st);
+    if (need <= 64) return launch_subwarp<T, 8, 8>(x, y, rows, cols, st);
+    if (need <= 128) return launch_subwarp<T, 8, 16>(x, y, rows, cols, st);
+  }
   if (version == 1) {
     if (warp_rv) return launch_warp_reg<T>(x, y, rows, cols, warp_rv, st);
     const int64_t blocks = (rows + kWarpRowsPerBlock - 1) / kWarpRowsPerBlock;
