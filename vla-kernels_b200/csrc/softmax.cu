@@ -18,9 +18,11 @@
 // vector body and a scalar tail. When x and y disagree modulo 16 bytes (an
 // offset view), all versions fall back to the scalar online kernel.
 //
-// fp32 / fp64 (computed in fp32 like the reference's dispatch body): x - max is formed in fp32 exactly as torch does, exp is the accurate
-// expf and the normalisation is an IEEE division, which keeps the fp32 result
-// within 1e-6 relative of the exact value. fp16 / bf16: exp2 on the MUFU unit.
+// fp32 / fp64 (computed in fp32 like the reference's dispatch body): x - max
+// is formed in fp32 exactly as torch does, exp is the accurate expf and the
+// normalisation multiplies by the IEEE-rounded reciprocal of the row sum, which
+// keeps the fp32 result within 1e-6 relative of the exact value. fp16 / bf16:
+// exp2 on the MUFU unit.
 // A row of all -inf yields NaN, as torch.softmax does.
 
 #include <cuda_bf16.h>
@@ -47,14 +49,12 @@ template <> __device__ __forceinline__ float exp_shift<float>(float x, float m) 
 template <> __device__ __forceinline__ float exp_shift<double>(float x, float m) {
   return expf(x - m);
 }
+// e / s as e times the row's reciprocal. `inv` is 1.f / s, an IEEE-rounded
+// division done once per row, so the result is within about one ulp of the
+// correctly rounded quotient (the fp32 bar is 1e-6 relative) at the cost of
+// one multiply per element instead of a division.
 template <typename T> __device__ __forceinline__ float normalize(float e, float s, float inv) {
   return e * inv;
-}
-template <> __device__ __forceinline__ float normalize<float>(float e, float s, float inv) {
-  return __fdiv_rn(e, s);
-}
-template <> __device__ __forceinline__ float normalize<double>(float e, float s, float inv) {
-  return __fdiv_rn(e, s);
 }
 
 // Segmentation of one row into scalar head, 16-byte body, scalar tail.
