@@ -14,31 +14,34 @@
 // The G query heads of a kv head share K/V, so an item stacks its rows as
 // r = m_local * G + g (the order in which q stores them) into up to two
 // 128-row M-tiles; K/V are read once per item and reused by all G heads.
-// Items are distributed over a persistent grid of one CTA per SM.
+// Items are distributed over a persistent grid of two CTAs per SM; the two
+// CTAs' chunk pipelines are independent and fill each other's stalls.
 //
-// Roles inside a CTA (12 warps = 3 warpgroups):
+// Roles inside a CTA (10 warps):
 //   warps 0-3   softmax for M-tile 0, one TMEM lane (query row) per thread
 //   warps 4-7   softmax for M-tile 1
-//   warps 8-9   idle
-//   warp 10     TMA producer: Q tiles (double-buffered across items) and
-//               64-key K/V chunks through an 8-stage ring.
-//   warp 11     TMEM allocator and MMA issuer (one elected lane):
+//   warp 8      TMA producer: Q tiles into two buffers (items alternate) and
+//               64-key K/V chunks through a 3-stage ring
+//   warp 9      TMEM allocator and MMA issuer (one elected lane):
 //               S_t = Q_t K_c^T  (SS MMA, M=128, N=chunk width, K=64)
 //               O_t (+)= P_t V_c (TS MMA: P from TMEM, V from smem, N=64)
-// Keys are processed in 64-key chunks; S and P are double-buffered, so the
-// MMA warp computes S two chunks ahead while softmax turns the current chunk
-// into P. A softmax thread reads its row of a chunk's S from TMEM once
-// (2 x 32 columns).
+// Keys are processed in 64-key chunks. Softmax writes P over the columns of S
+// it has read; the MMA warp then issues P.V and, behind it in issue order,
+// the next chunk's S into the same columns.
 //
-// Tensor memory (512 columns x 128 lanes, fp32 cells), per M-tile t at 256 t:
-//   [0,64) [64,128) S buffers   [128,160) [160,192) P buffers   [192,256) O
-// P holds bf16 pairs (two keys per 32-bit column), the A-operand layout of
-// the TS MMA.
+// Tensor memory (256 columns x 128 lanes per CTA, fp32 cells), per M-tile t
+// at 128 t: [0,64) S, with P (bf16 pairs, two keys per 32-bit column, the
+// A-operand layout of the TS MMA) over its first 32 columns; [64,128) O.
+//
+// Output. When an item's O is final, its softmax warps write the bf16 rows
+// into the item's Q buffer (no longer read by then) and one thread per tile
+// stores the tile with a TMA tensor store; the buffer goes back to the
+// producer once the store has read it.
 //
 // Online softmax in the exp2 domain with a lazily updated row max: the
-// reference max only moves (and O / l are rescaled in TMEM) when a new chunk's
-// max exceeds it by more than 8 (a factor 256), so P stays <= 256 in bf16 and
-// rescales are rare.
+// reference max only moves (and O / l are rescaled in TMEM) when a new
+// group's max exceeds it by more than 8 (a factor 256), so P stays <= 256 in
+// bf16 and rescales are rare.
 //
 // Every mbarrier wait is bounded (1 s); on expiry the kernel records
 // VLAK_ERR_DEVICE_TIMEOUT in the device error word, drains its own TMA and
@@ -126,15 +129,25 @@ constexpr int kWarpProducer = 8, kWarpMma = 9;
 #endif
 constexpr uint32_t kPolyMask = VLAK_POLY_MASK;
 constexpr int kChunk = 64;      // keys per K/V chunk (S tile width)
-constexpr int kStages = 4;      // K/V ring depth (chunks) per CTA
+constexpr int kStages = 3;      // K/V ring depth (chunks) per CTA
 constexpr int kRowBytes = 128;  // 64 bf16 per row
 constexpr int kTileBytes = 128 * kRowBytes;        // one 128-row Q tile
 constexpr int kChunkBytes = kChunk * kRowBytes;    // one 64-key K (or V) chunk
 constexpr int kQBytes = 2 * kTileBytes;            // the 2 M-tiles of one item
 constexpr int kKVBytes = kStages * kChunkBytes;    // K ring (V ring the same)
-constexpr int kSmemData = kQBytes + 2 * kKVBytes;  // 96 KB
+// Two Q buffers (items alternate between them). A finished item's buffer
+// then stages its O rows for the TMA store.
+constexpr int kSmemData = 2 * kQBytes + 2 * kKVBytes;  // 112 KB
 constexpr int kBarrierBytes = 256;
-constexpr int kSmemBytes = kSmemData + kBarrierBytes + 1024;  // + alignment slack
+// The operand tiles need 1024-byte alignment and the dynamic shared memory
+// base is only guaranteed 16-byte aligned. The barrier block goes into the
+// alignment gap when the gap has room for it and after the data otherwise,
+// so 1008 bytes of slack cover every base alignment: two CTAs then fit in an
+// SM's 228 KB (each CTA also has 1 KB reserved by the system).
+constexpr int kSmemSlack = 1008;
+constexpr int kSmemBytes = kSmemData + kSmemSlack;
+static_assert(kBarrierBytes + 240 <= kSmemSlack, "barrier block does not fit the slack");
+static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs must share an SM");
 
 // Tensor memory (256 columns per CTA), per M-tile t at 128 t: S [0,64) and O
 // [64,128). P (bf16 pairs, two keys per 32-bit column) is written over the
@@ -149,6 +162,7 @@ struct __align__(64) Params {
   CUtensorMap tm_q;  // dims (64, H, M, B), box (64, G, MT, 1)
   CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 64, 1)
   CUtensorMap tm_v;
+  CUtensorMap tm_o;  // dims (64, H, M, B), box (64, G, MT, 1), TMA stores of O
   __nv_bfloat16* o;
   long long o_sb, o_sm, o_sh;  // element strides of o
   int B, M, N, H, Hkv, G;
@@ -175,12 +189,13 @@ struct __align__(64) Params {
 constexpr int kMaskAnalytic = 0, kMaskLength = 1, kMaskBool = 2;
 
 struct Barriers {
-  uint64_t q_full, q_empty;
+  uint64_t q_full[2], q_empty[2];  // [Q buffer]
   uint64_t kv_full[kStages], kv_empty[kStages];
   uint64_t s_full[2];   // [tile]: S of the chunk is in TMEM
   uint64_t p_full[2];   // [tile]: the tile's 4 softmax warps wrote P
   uint64_t pv_done[2];  // [tile]: P.V of the chunk completed
   uint64_t o_full[2];   // [tile]: O of the item is final
+  uint64_t o_staged[2]; // [tile]: the tile's 4 softmax warps wrote O to smem
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -260,22 +275,27 @@ template <int kMode>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gqa_attention_sm100(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment for the 128-byte-swizzled operand tiles
+  // 1024-byte alignment for the 128-byte-swizzled operand tiles; the barrier
+  // block sits in the alignment gap when it fits there
   const uint32_t raw_addr = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* q_smem = smem;                      // [tile][128 x 128 B]
-  uint8_t* k_smem = smem + kQBytes;            // [stage][64 x 128 B]
+  const uint32_t gap = ((raw_addr + 1023u) & ~1023u) - raw_addr;
+  uint8_t* smem = smem_raw + gap;
+  uint8_t* q_smem = smem;                      // [Q buffer][tile][128 x 128 B]
+  uint8_t* k_smem = smem + 2 * kQBytes;        // [stage][64 x 128 B]
   uint8_t* v_smem = k_smem + kKVBytes;
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kSmemData);
+  Barriers* bars = reinterpret_cast<Barriers*>(gap >= kBarrierBytes ? smem_raw : smem + kSmemData);
   volatile int* abort_flag = &bars->abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full, 1);
-    mbar_init(&bars->q_empty, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->q_full[i], 1);
+      // one arrival per M-tile once its O has been read out of the buffer
+      // (tile 0 arrives twice for a one-tile item)
+      mbar_init(&bars->q_empty[i], 2);
+      mbar_init(&bars->o_staged[i], 4);  // one arrival per softmax warp of the tile
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp of the tile
       mbar_init(&bars->pv_done[i], 1);
@@ -295,7 +315,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   }
   // Q rows that no TMA box covers feed only discarded rows; clear them once so
   // they hold finite values.
-  for (int i = threadIdx.x; i < kQBytes / 16; i += kThreads)
+  for (int i = threadIdx.x; i < 2 * kQBytes / 16; i += kThreads)
     reinterpret_cast<uint4*>(q_smem)[i] = make_uint4(0, 0, 0, 0);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   tc_fence_before();
@@ -323,17 +343,19 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       // an item with no live chunk is written as zeros by the softmax warps
       // alone: no Q, no K/V, no barrier phase
       if (next_live<kMode>(p, it, 0, n_chunks) < 0) continue;
-      // the single Q buffer is free once the previous item's S products completed
-      if (!__all_sync(kFullMask, bounded_wait(&bars->q_empty, (qi & 1) ^ 1, abort_flag))) {
+      // Q buffer qi & 1 is free once the O rows that item qi - 2 staged in
+      // it have been stored
+      const uint32_t qb = qi & 1;
+      if (!__all_sync(kFullMask, bounded_wait(&bars->q_empty[qb], ((qi >> 1) & 1) ^ 1, abort_flag))) {
         ok = false;
         break;
       }
       const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
-      mbar_arrive_expect_tx_elect(&bars->q_full, qbytes);
+      mbar_arrive_expect_tx_elect(&bars->q_full[qb], qbytes);
       ++q_armed;
       for (int t = 0; t < it.tiles_active; ++t)
-        tma_load_4d_elect(q_smem + t * kTileBytes, &p.tm_q, &bars->q_full, 0, it.kvh * p.G,
-                          it.m0 + t * p.MT, it.b);
+        tma_load_4d_elect(q_smem + qb * kQBytes + t * kTileBytes, &p.tm_q, &bars->q_full[qb], 0,
+                          it.kvh * p.G, it.m0 + t * p.MT, it.b);
       for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks)) {
         const int s = kv % kStages;
         if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
@@ -351,7 +373,11 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     }
     // never leave the CTA with copies in flight: wait for the last phase
     // armed on every full barrier (bounded, independent of the abort flag)
-    if (q_armed > 0) bounded_wait(&bars->q_full, (q_armed - 1) & 1, abort_flag, false);
+    // buffer b was armed (q_armed + 1 - b) / 2 times
+    for (uint32_t b = 0; b < 2; ++b) {
+      const uint32_t uses = (q_armed + 1 - b) / 2;
+      if (uses > 0) bounded_wait(&bars->q_full[b], (uses - 1) & 1, abort_flag, false);
+    }
     for (int s = 0; s < kStages; ++s)
       if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
     __syncwarp();
@@ -369,12 +395,12 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         const Item it = decode_item<kMode>(p, item);
         const bool two = it.tiles_active == 2;
         if (next_live<kMode>(p, it, 0, n_chunks) < 0) continue;  // zeros, written by softmax
-        if (!__all_sync(kFullMask, bounded_wait(&bars->q_full, qi & 1, abort_flag))) {
+        if (!__all_sync(kFullMask, bounded_wait(&bars->q_full[qi & 1], (qi >> 1) & 1, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t q_base = smem_u32(q_smem);
+        const uint32_t q_base = smem_u32(q_smem + (qi & 1) * kQBytes);
         auto issue_s = [&](int t, int c, int j) {  // four K16 steps, 32 B apart in a swizzled row
           const int s = (kv + j) % kStages;
           const uint32_t idesc = idesc_bf16_f32(128, chunk_cols(p, c), false);
@@ -424,7 +450,6 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         if (two) issue_s(1, cur, 0);
         while (cur >= 0) {
           const int nxt = next_live<kMode>(p, it, cur + 1, n_chunks);
-          if (nxt < 0) umma_commit_elect(&bars->q_empty);  // the item's last S products read Q
           // per tile: P of chunk j ready -> O += P V(j), then S of chunk j+1
           // over the S/P columns (in issue order after the product reading P)
           if (!wait_p(0)) { ok = false; break; }
@@ -469,10 +494,27 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     const int m_local = row / p.G;
     const int g = row - m_local * p.G;
     uint32_t sph = 0, oph = 0, pv_seen = 0;  // pv_seen: this tile's P.V products so far
+    uint32_t qi = 0;    // items with live chunks so far; item qi uses Q buffer qi & 1
+    // Quarter-0 warps: the Q buffer whose staged O rows this tile's last TMA
+    // store reads, (buffer + 1) | (q_empty arrivals << 2), or 0. The buffer is
+    // handed back to the producer one chunk later, when the store has long
+    // finished reading it, or at once when the warp has no chunk to process.
+    uint32_t pend = 0;
+    auto release = [&]() {
+      if (lane == 0) {
+        bulk_wait_read0();
+        mbar_arrive_count(&bars->q_empty[(pend & 3u) - 1u], pend >> 2);
+      }
+      pend = 0;
+    };
     bool ok = true;
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
       const Item it = decode_item<kMode>(p, item);
+      const bool live = next_live<kMode>(p, it, 0, n_chunks) >= 0;
+      const uint32_t qb = qi & 1;
+      qi += live ? 1u : 0u;
+      if (pend != 0 && (t >= it.tiles_active || !live)) release();
       if (t >= it.tiles_active) continue;
       const int m_first = it.m0 + t * p.MT;        // first query position of this tile
       const int m = m_first + m_local;
@@ -489,12 +531,12 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       const uint8_t* mrow = nullptr;
       if (kMode == kMaskBool && valid)
         mrow = p.mask + static_cast<long long>(it.b) * p.mask_sb + static_cast<long long>(m) * p.mask_sm;
-      __nv_bfloat16* orow = p.o + static_cast<long long>(it.b) * p.o_sb +
-                            static_cast<long long>(m) * p.o_sm +
-                            static_cast<long long>(it.kvh * p.G + g) * p.o_sh;
-      if (next_live<kMode>(p, it, 0, n_chunks) < 0) {
+      if (!live) {
         // no key visible to any row of the item: zeros, no barrier phase
         if (valid) {
+          __nv_bfloat16* orow = p.o + static_cast<long long>(it.b) * p.o_sb +
+                                static_cast<long long>(m) * p.o_sm +
+                                static_cast<long long>(it.kvh * p.G + g) * p.o_sh;
 #pragma unroll
           for (int v = 0; v < 8; ++v) reinterpret_cast<uint4*>(orow)[v] = make_uint4(0, 0, 0, 0);
         }
@@ -661,13 +703,18 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         ++pv_seen;
         tc_fence_before();
         mbar_arrive_elect(&bars->p_full[t], 1u);
+        if (pend != 0) release();
       }
       if (!ok) break;
-      // epilogue: O / l -> bf16 rows, written from registers (each thread one
-      // 128-byte row of o)
+      // Epilogue: O / l -> bf16 rows staged in this item's Q buffer (dead once
+      // O is final: every MMA of the item has completed), in the 128-byte
+      // swizzled layout of the Q / O tensor maps, then one TMA store per tile.
+      // Per-thread global stores of whole rows (one 128-byte line per lane)
+      // flood the SM's memory pipeline and stall the barrier waits behind it.
       if (!__all_sync(kFullMask, bounded_wait(&bars->o_full[t], oph, abort_flag))) { ok = false; break; }
       oph ^= 1;
       tc_fence_after();
+      uint8_t* stage = q_smem + qb * kQBytes + t * kTileBytes;
       if (warp_active) {
         const bool any = (j > 0) && (l_run > 0.f);
         const float inv = any ? 1.f / l_run : 0.f;
@@ -685,15 +732,32 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
 #pragma unroll
               for (int e = 0; e < 4; ++e)
                 w[e] = any ? pack_bf16x2(o[v * 8 + 2 * e] * inv, o[v * 8 + 2 * e + 1] * inv) : 0u;
-              *reinterpret_cast<uint4*>(orow + q4 * 16 + v * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+              const uint32_t chunk = static_cast<uint32_t>(2 * q4 + v) ^ static_cast<uint32_t>(row & 7);
+              st_shared_v4(stage + row * kRowBytes + chunk * 16, w[0], w[1], w[2], w[3]);
             }
           }
         }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive_elect(&bars->o_staged[t], 1u);
+      if (quarter == 0) {
+        // o_staged completes one phase per item of the tile, like o_full
+        if (!__all_sync(kFullMask, bounded_wait(&bars->o_staged[t], oph ^ 1u, abort_flag))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          tma_store_4d(&p.tm_o, stage, 0, it.kvh * p.G, m_first, it.b);
+          bulk_commit_group();
+        }
+        pend = (qb + 1u) | ((t == 0 && it.tiles_active == 1 ? 2u : 1u) << 2);
       }
       // the next item's first P.V overwrites O once this tile's softmax warps
       // arrive on p_full, after these loads
       tc_fence_before();
     }
+    // the TMA stores of this warp's last items complete before the CTA exits
+    if (quarter == 0 && lane == 0) bulk_wait_all0();
   }
 
   tc_fence_before();
@@ -886,6 +950,9 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
 
   st = encode_map(&prm.tm_q, a->q, a->H, a->M, a->B, a->q_stride[2], a->q_stride[1],
                   a->q_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "q");
+  if (st != VLAK_OK) return st;
+  st = encode_map(&prm.tm_o, a->o, a->H, a->M, a->B, a->o_stride[2], a->o_stride[1],
+                  a->o_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "o");
   if (st != VLAK_OK) return st;
   st = encode_map(&prm.tm_k, a->k, a->Hkv, a->N, a->B, a->k_stride[2], a->k_stride[1],
                   a->k_stride[0], 1, kChunk, "k");

@@ -389,6 +389,17 @@ __device__ __forceinline__ void tma_load_4d_elect(void* smem_dst, const CUtensor
       : "memory");
 }
 
+__device__ __forceinline__ void st_shared_v4(void* dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_count(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count)
+               : "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulator.
 // Bit fields: [4,6) D format (1 = f32), [7,10) A format (1 = bf16),
 // [10,13) B format (1 = bf16), 15 A major (0 = K), 16 B major (1 = MN),
