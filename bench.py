@@ -336,12 +336,43 @@ def time_calls(fn, calls: int, warmup: int = 5) -> float:
     return e0.elapsed_time(e1) / 1e3 / calls
 
 
+def time_graph(fns, replays: int = 5) -> float:
+    """Mean seconds per call of the calls fns (each a zero-argument launch)
+    captured once into a CUDA graph and replayed: device time without the
+    host's per-call dispatch."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for f in fns[:3]:
+            f()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in fns:
+            f()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) / 1e3 / (replays * len(fns))
+
+
 def bench_sites():
     """Per-call times of the other attention sites on one GPU (reported, not
     the headline): C3 expert self-attention at B = 1, 8, 64, C4 prefix
     attention with per-sample lengths at B = 1, 16, 128, and the SigLIP
     vision site (1, 12, 1024, 64) through vlak::fused_attention beside torch
-    SDPA. Inputs rotate over enough sets to exceed L2 where a call is small."""
+    SDPA. Inputs rotate over enough sets to exceed L2 where a call is small.
+    "us" is eager (each call dispatched from Python, host overhead included
+    when the kernel is shorter than the dispatch); "graph_us" replays the same
+    calls from a CUDA graph (device time)."""
     import torch.nn.functional as F
 
     from kernels.attention import (fused_attention, fused_attention_gqa_v4,
@@ -361,7 +392,9 @@ def bench_sites():
             fused_attention_gqa_v4(q, k, v, scale=0.125, prefix_len=s.P)
 
         t = time_calls(call, 200)
-        res[f"C3_B{B}"] = {"us": round(t * 1e6, 2),
+        tg = time_graph([lambda i=i: fused_attention_gqa_v4(*sets[i % nsets], scale=0.125,
+                                                             prefix_len=s.P) for i in range(32)])
+        res[f"C3_B{B}"] = {"us": round(t * 1e6, 2), "graph_us": round(tg * 1e6, 2),
                            "GB/s": round(wl.attn_bytes(s) / t / 1e9, 1),
                            "TFLOP/s": round(wl.attn_flops(s) / t / 1e12, 2),
                            "tensor_frac": round(wl.attn_flops(s) / t / 1e12 / peaks["bf16_tflops"], 4),
@@ -380,7 +413,9 @@ def bench_sites():
             fused_attention_gqa_varlen(q, k, v, L)
 
         t = time_calls(call, 100)
-        res[f"C4_varlen_B{B}"] = {"us": round(t * 1e6, 2),
+        tg = time_graph([lambda i=i: fused_attention_gqa_varlen(*sets[i % nsets], L)
+                         for i in range(32)])
+        res[f"C4_varlen_B{B}"] = {"us": round(t * 1e6, 2), "graph_us": round(tg * 1e6, 2),
                                   "GB/s": round(wl.attn_bytes(s) / t / 1e9, 1),
                                   "TFLOP/s": round(wl.varlen_flops(L) / t / 1e12, 2),
                                   "input_sets": nsets}
@@ -389,9 +424,12 @@ def bench_sites():
     flops = 4 * 64 * 12 * 1024 * 1024
     t_ours = time_calls(lambda: fused_attention(q, k, v), 100)
     t_sdpa = time_calls(lambda: F.scaled_dot_product_attention(q, k, v), 100)
-    res["SigLIP_1x12x1024"] = {"us": round(t_ours * 1e6, 2),
-                               "TFLOP/s": round(flops / t_ours / 1e12, 1),
-                               "torch_sdpa_us": round(t_sdpa * 1e6, 2)}
+    g_ours = time_graph([lambda: fused_attention(q, k, v)] * 32)
+    g_sdpa = time_graph([lambda: F.scaled_dot_product_attention(q, k, v)] * 32)
+    res["SigLIP_1x12x1024"] = {"us": round(t_ours * 1e6, 2), "graph_us": round(g_ours * 1e6, 2),
+                               "TFLOP/s": round(flops / g_ours / 1e12, 1),
+                               "torch_sdpa_us": round(t_sdpa * 1e6, 2),
+                               "torch_sdpa_graph_us": round(g_sdpa * 1e6, 2)}
     return res
 
 

@@ -157,6 +157,33 @@ VLAK_API int vlak_attn_gqa_masked_fwd(const vlak_attn_gqa_args* args, const void
                                       int64_t mask_stride_b, int64_t mask_stride_m,
                                       void* stream);
 
+/* Key-split variants for small batches. No counterpart in the reference,
+ * whose v3 launches one CTA per (b, head, 32- or 64-row query tile) however
+ * few that makes (kernels/attention/fused_attention.cu:646-663). When the
+ * query blocks fill
+ * less than half of the GPU, these split each block's keys across CTAs and
+ * merge the partial results with a second kernel on `stream`; they need a
+ * device workspace of vlak_attn_gqa_workspace_size bytes, 256-byte aligned,
+ * owned by the caller and not used by anything else until the work on
+ * `stream` has finished. A NULL or smaller workspace runs unsplit. Results
+ * match the unsplit calls within bf16 rounding (each split's O / l is held
+ * in bf16 before the merge). */
+/* Workspace bytes a _ws call with these arguments uses on the current
+ * device (0 when it would not split). Validates like vlak_attn_gqa_check. */
+VLAK_API int vlak_attn_gqa_workspace_size(const vlak_attn_gqa_args* args, int64_t* bytes);
+/* vlak_attn_gqa_fwd with a workspace (also serves _v4). */
+VLAK_API int vlak_attn_gqa_fwd_ws(const vlak_attn_gqa_args* args, void* workspace,
+                                  int64_t workspace_bytes, void* stream);
+/* vlak_attn_gqa_varlen_fwd with a workspace. */
+VLAK_API int vlak_attn_gqa_varlen_fwd_ws(const vlak_attn_gqa_args* args, const void* lengths,
+                                         int lengths_dtype, void* workspace,
+                                         int64_t workspace_bytes, void* stream);
+/* vlak_attn_gqa_masked_fwd with a workspace. */
+VLAK_API int vlak_attn_gqa_masked_fwd_ws(const vlak_attn_gqa_args* args, const void* mask,
+                                         int64_t mask_stride_b, int64_t mask_stride_m,
+                                         void* workspace, int64_t workspace_bytes,
+                                         void* stream);
+
 /* Non-GQA attention on the CUDA cores with fp32 math: the v1 path of
  * vlak::fused_attention for fp32 / fp16 / fp64 inputs (replaces
  * fused_attention_warp_row and its host branch,

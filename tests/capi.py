@@ -48,6 +48,19 @@ def lib():
     L.vlak_attn_gqa_check.argtypes = [ctypes.POINTER(GqaArgs), ctypes.POINTER(ctypes.c_int64),
                                       ctypes.POINTER(ctypes.c_float)]
     L.vlak_device_error_read.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    L.vlak_attn_gqa_workspace_size.argtypes = [ctypes.POINTER(GqaArgs), ctypes.POINTER(ctypes.c_int64)]
+    L.vlak_attn_gqa_fwd_ws.argtypes = [ctypes.POINTER(GqaArgs), ctypes.c_void_p, ctypes.c_int64,
+                                       ctypes.c_void_p]
+    L.vlak_attn_gqa_varlen_fwd.argtypes = [ctypes.POINTER(GqaArgs), ctypes.c_void_p, ctypes.c_int,
+                                           ctypes.c_void_p]
+    L.vlak_attn_gqa_varlen_fwd_ws.argtypes = [ctypes.POINTER(GqaArgs), ctypes.c_void_p,
+                                              ctypes.c_int, ctypes.c_void_p, ctypes.c_int64,
+                                              ctypes.c_void_p]
+    L.vlak_attn_gqa_masked_fwd.argtypes = [ctypes.POINTER(GqaArgs), ctypes.c_void_p,
+                                           ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+    L.vlak_attn_gqa_masked_fwd_ws.argtypes = [ctypes.POINTER(GqaArgs), ctypes.c_void_p,
+                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                              ctypes.c_int64, ctypes.c_void_p]
     L.vlak_selftest_wait_timeout.argtypes = [ctypes.c_void_p]
     return L
 
@@ -93,6 +106,62 @@ def attn_gqa(q, k, v, prefix_len=-1, dead_start=0, dead_end=0, scale=-1.0, v4=Fa
     a = gqa_args(q, k, v, o, prefix_len, dead_start, dead_end, scale)
     f = L.vlak_attn_gqa_v4_fwd if v4 else L.vlak_attn_gqa_fwd
     st = f(ctypes.byref(a), stream_ptr())
+    return st, o
+
+
+def workspace_size(q, k, v, prefix_len=-1, dead_start=0, dead_end=0) -> int:
+    """Bytes the key-split (_ws) entry points want for these arguments."""
+    B, M, H, D = q.shape
+    o = torch.empty(B, M, H, D, device=q.device, dtype=torch.bfloat16)
+    a = gqa_args(q, k, v, o, prefix_len, dead_start, dead_end)
+    n = ctypes.c_int64(-1)
+    st = lib().vlak_attn_gqa_workspace_size(ctypes.byref(a), ctypes.byref(n))
+    assert st == VLAK_OK, last_error()
+    return n.value
+
+
+def attn_gqa_ws(q, k, v, prefix_len=-1, dead_start=0, dead_end=0, scale=-1.0, lengths=None,
+                mask=None, workspace=None):
+    """Run the GQA kernel through a key-split (_ws) entry point with a
+    workspace of the size the library asks for (or the given one); lengths
+    selects the varlen form, mask (B, M, N bool) the masked form. Returns
+    (status, o)."""
+    L = lib()
+    B, M, H, D = q.shape
+    o = torch.empty(B, M, H, D, device=q.device, dtype=torch.bfloat16)
+    a = gqa_args(q, k, v, o, prefix_len, dead_start, dead_end, scale)
+    if workspace is None:
+        n = ctypes.c_int64(0)
+        assert L.vlak_attn_gqa_workspace_size(ctypes.byref(a), ctypes.byref(n)) == VLAK_OK
+        workspace = torch.empty(max(n.value, 1), device=q.device, dtype=torch.uint8)
+    wp, wn = workspace.data_ptr(), workspace.numel()
+    if lengths is not None:
+        dt = 5 if lengths.dtype == torch.int64 else 4
+        st = L.vlak_attn_gqa_varlen_fwd_ws(ctypes.byref(a), lengths.data_ptr(), dt, wp, wn,
+                                           stream_ptr())
+    elif mask is not None:
+        N = k.shape[1]
+        st = L.vlak_attn_gqa_masked_fwd_ws(ctypes.byref(a), mask.data_ptr(), M * N, N, wp, wn,
+                                           stream_ptr())
+    else:
+        st = L.vlak_attn_gqa_fwd_ws(ctypes.byref(a), wp, wn, stream_ptr())
+    return st, o
+
+
+def attn_gqa_plain(q, k, v, lengths=None, mask=None, prefix_len=-1, dead_start=0, dead_end=0):
+    """The unsplit entry points (varlen / masked / analytic)."""
+    L = lib()
+    B, M, H, D = q.shape
+    o = torch.empty(B, M, H, D, device=q.device, dtype=torch.bfloat16)
+    a = gqa_args(q, k, v, o, prefix_len, dead_start, dead_end)
+    if lengths is not None:
+        dt = 5 if lengths.dtype == torch.int64 else 4
+        st = L.vlak_attn_gqa_varlen_fwd(ctypes.byref(a), lengths.data_ptr(), dt, stream_ptr())
+    elif mask is not None:
+        N = k.shape[1]
+        st = L.vlak_attn_gqa_masked_fwd(ctypes.byref(a), mask.data_ptr(), M * N, N, stream_ptr())
+    else:
+        st = L.vlak_attn_gqa_fwd(ctypes.byref(a), stream_ptr())
     return st, o
 
 

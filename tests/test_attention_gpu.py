@@ -294,7 +294,11 @@ def test_through_c_abi(v4):
     assert st == capi.VLAK_OK, capi.last_error()
     torch.cuda.synchronize()
     check(o, oracle(q, k, v, 241, 196, 240))
-    assert torch.equal(o, fused_attention_gqa(q, k, v, prefix_len=241, dead_start=196, dead_end=240))
+    # the torch op runs the key-split form at this small batch: same result
+    # through the C ABI's workspace entry point
+    st, o_ws = capi.attn_gqa_ws(q, k, v, prefix_len=241, dead_start=196, dead_end=240)
+    assert st == capi.VLAK_OK, capi.last_error()
+    assert torch.equal(o_ws, fused_attention_gqa(q, k, v, prefix_len=241, dead_start=196, dead_end=240))
 
 
 def test_device_error_word_stays_clear():

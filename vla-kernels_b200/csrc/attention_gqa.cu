@@ -163,6 +163,13 @@ struct __align__(64) Params {
   CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 64, 1)
   CUtensorMap tm_v;
   CUtensorMap tm_o;  // dims (64, H, M, B), box (64, G, MT, 1), TMA stores of O
+  // Key splits (splits > 1): split s of a query block covers chunks
+  // [s * split_chunks, (s + 1) * split_chunks) and writes O / l in bf16 to the
+  // partials (dims (64, H, M, splits * B), box as tm_o) and (reference max,
+  // row sum) to part_ml; a combine kernel then writes o.
+  CUtensorMap tm_part;
+  float2* part_ml;
+  int splits, split_chunks, n_chunks;
   __nv_bfloat16* o;
   long long o_sb, o_sm, o_sh;  // element strides of o
   int B, M, N, H, Hkv, G;
@@ -207,13 +214,19 @@ struct Item {
   int b, kvh, m0;  // m0: first query position of the item
   int tiles_active;
   int L;           // mask mode 1: length of sample b
+  int split;       // key split of the item
+  int c_begin, c_end;  // key chunks [c_begin, c_end) of the split
 };
 
-template <int kMode>
+template <int kMode, bool kSplit>
 __device__ __forceinline__ Item decode_item(const Params& p, int item) {
   Item it;
-  const int mblk = item % p.n_mblk;
-  const int bk = item / p.n_mblk;
+  it.split = kSplit ? item % p.splits : 0;
+  const int qblk = kSplit ? item / p.splits : item;
+  it.c_begin = kSplit ? it.split * p.split_chunks : 0;
+  it.c_end = kSplit ? min(p.n_chunks, it.c_begin + p.split_chunks) : p.n_chunks;
+  const int mblk = qblk % p.n_mblk;
+  const int bk = qblk / p.n_mblk;
   it.kvh = bk % p.Hkv;
   it.b = bk / p.Hkv;
   it.m0 = mblk * p.tiles * p.MT;
@@ -240,11 +253,17 @@ __device__ __forceinline__ bool chunk_live(const Params& p, const Item& it, int 
   const int e2_hi = max(p.P, min(p.N, p.N - p.M + m_hi + 1));
   return (c0 < p.ds) || (c0 + width > p.de && c0 < e2_hi);
 }
-template <int kMode>
-__device__ __forceinline__ int next_live(const Params& p, const Item& it, int c, int n_chunks) {
-  for (; c < n_chunks; ++c)
+// First live chunk at or after c within the item's split, or -1.
+template <int kMode, bool kSplit>
+__device__ __forceinline__ int next_live(const Params& p, const Item& it, int c) {
+  const int end = kSplit ? it.c_end : p.n_chunks;
+  for (; c < end; ++c)
     if (chunk_live<kMode>(p, it, c)) return c;
   return -1;
+}
+template <int kMode, bool kSplit>
+__device__ __forceinline__ int first_live(const Params& p, const Item& it) {
+  return next_live<kMode, kSplit>(p, it, kSplit ? it.c_begin : 0);
 }
 
 // Bits of keys g0 .. g0+31 of one bool-mask row (bit i set when key g0 + i is
@@ -271,7 +290,7 @@ __device__ __forceinline__ int chunk_cols(const Params& p, int c) {
   return (width + 15) & ~15;  // MMA N must be a multiple of 16
 }
 
-template <int kMode>
+template <int kMode, bool kSplit>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gqa_attention_sm100(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -322,7 +341,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const int n_chunks = (p.N + kChunk - 1) / kChunk;
+  // the merge kernel that follows a split launch may be scheduled from now
+  // on; it waits for this grid's completion before reading anything
+  if (kSplit) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------ producer
@@ -339,10 +360,10 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     uint32_t kv_used = 0, kv_par = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
-      const Item it = decode_item<kMode>(p, item);
+      const Item it = decode_item<kMode, kSplit>(p, item);
       // an item with no live chunk is written as zeros by the softmax warps
       // alone: no Q, no K/V, no barrier phase
-      if (next_live<kMode>(p, it, 0, n_chunks) < 0) continue;
+      if (first_live<kMode, kSplit>(p, it) < 0) continue;
       // Q buffer qi & 1 is free once the O rows that item qi - 2 staged in
       // it have been stored
       const uint32_t qb = qi & 1;
@@ -356,7 +377,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       for (int t = 0; t < it.tiles_active; ++t)
         tma_load_4d_elect(q_smem + qb * kQBytes + t * kTileBytes, &p.tm_q, &bars->q_full[qb], 0,
                           it.kvh * p.G, it.m0 + t * p.MT, it.b);
-      for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks)) {
+      for (int c = first_live<kMode, kSplit>(p, it); c >= 0; c = next_live<kMode, kSplit>(p, it, c + 1)) {
         const int s = kv % kStages;
         if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
           ok = false;
@@ -392,9 +413,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       uint32_t pph = 0;  // bit t: parity expected on p_full[t]
       bool ok = true;
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
-        const Item it = decode_item<kMode>(p, item);
+        const Item it = decode_item<kMode, kSplit>(p, item);
         const bool two = it.tiles_active == 2;
-        if (next_live<kMode>(p, it, 0, n_chunks) < 0) continue;  // zeros, written by softmax
+        if (first_live<kMode, kSplit>(p, it) < 0) continue;  // zeros, written by softmax
         if (!__all_sync(kFullMask, bounded_wait(&bars->q_full[qi & 1], (qi >> 1) & 1, abort_flag))) {
           ok = false;
           break;
@@ -440,7 +461,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           tc_fence_after();
           return true;
         };
-        int cur = next_live<kMode>(p, it, 0, n_chunks);
+        int cur = first_live<kMode, kSplit>(p, it);
         int j = 0;
         // S of chunk 0 is issued after the previous item's last P.V, which
         // read P from the same columns; tcgen05.mma operations of one thread
@@ -449,7 +470,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         issue_s(0, cur, 0);
         if (two) issue_s(1, cur, 0);
         while (cur >= 0) {
-          const int nxt = next_live<kMode>(p, it, cur + 1, n_chunks);
+          const int nxt = next_live<kMode, kSplit>(p, it, cur + 1);
           // per tile: P of chunk j ready -> O += P V(j), then S of chunk j+1
           // over the S/P columns (in issue order after the product reading P)
           if (!wait_p(0)) { ok = false; break; }
@@ -510,8 +531,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     bool ok = true;
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
-      const Item it = decode_item<kMode>(p, item);
-      const bool live = next_live<kMode>(p, it, 0, n_chunks) >= 0;
+      const Item it = decode_item<kMode, kSplit>(p, item);
+      const bool live = first_live<kMode, kSplit>(p, it) >= 0;
       const uint32_t qb = qi & 1;
       qi += live ? 1u : 0u;
       if (pend != 0 && (t >= it.tiles_active || !live)) release();
@@ -531,9 +552,17 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       const uint8_t* mrow = nullptr;
       if (kMode == kMaskBool && valid)
         mrow = p.mask + static_cast<long long>(it.b) * p.mask_sb + static_cast<long long>(m) * p.mask_sm;
+      // this thread's (b, m, h) row in the split partials (computed where
+      // used, so it is not live across the chunk loop)
+      auto part_row = [&]() {
+        return ((static_cast<long long>(it.split) * p.B + it.b) * p.M + m) * p.H + it.kvh * p.G + g;
+      };
       if (!live) {
-        // no key visible to any row of the item: zeros, no barrier phase
-        if (valid) {
+        // no key visible to any row of the item: zeros, no barrier phase (a
+        // split records an empty partial, which the combine skips)
+        if (valid && kSplit) {
+          p.part_ml[part_row()] = make_float2(-INFINITY, 0.f);
+        } else if (valid) {
           __nv_bfloat16* orow = p.o + static_cast<long long>(it.b) * p.o_sb +
                                 static_cast<long long>(m) * p.o_sm +
                                 static_cast<long long>(it.kvh * p.G + g) * p.o_sh;
@@ -544,7 +573,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       }
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
-      for (int c = next_live<kMode>(p, it, 0, n_chunks); c >= 0; c = next_live<kMode>(p, it, c + 1, n_chunks), ++j) {
+      for (int c = first_live<kMode, kSplit>(p, it); c >= 0; c = next_live<kMode, kSplit>(p, it, c + 1), ++j) {
         // warp-uniform outcome: the TMEM accesses below are warp-collective
         if (!__all_sync(kFullMask, bounded_wait<kWaitSoftmax>(&bars->s_full[t], sph, abort_flag))) {
           ok = false;
@@ -738,6 +767,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           }
         }
       }
+      if (kSplit && valid) p.part_ml[part_row()] = make_float2(m_run, l_run);
       fence_proxy_async_smem();
       mbar_arrive_elect(&bars->o_staged[t], 1u);
       if (quarter == 0) {
@@ -747,7 +777,10 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           break;
         }
         if (lane == 0) {
-          tma_store_4d(&p.tm_o, stage, 0, it.kvh * p.G, m_first, it.b);
+          if (kSplit)
+            tma_store_4d(&p.tm_part, stage, 0, it.kvh * p.G, m_first, it.split * p.B + it.b);
+          else
+            tma_store_4d(&p.tm_o, stage, 0, it.kvh * p.G, m_first, it.b);
           bulk_commit_group();
         }
         pend = (qb + 1u) | ((t == 0 && it.tiles_active == 1 ? 2u : 1u) << 2);
@@ -779,6 +812,52 @@ __global__ void zero_rows(__nv_bfloat16* o, long long o_sb, long long o_sm, long
 #pragma unroll
     for (int v = 0; v < 8; ++v) row[v] = make_uint4(0, 0, 0, 0);
   }
+}
+
+// Merge of the key splits: eight threads per row of o, eight bf16 each. Split
+// s of a row holds O_s / l_s (bf16) and (m_s, l_s): its rows' probabilities
+// are 2^(x - m_s) and l_s their sum, so the whole row's sum is
+// sum_s l_s 2^(m_s - m*) (any common m*) and O = sum_s w_s (O_s / l_s) /
+// sum_s w_s with w_s = l_s 2^(m_s - m*). Splits with l_s = 0 saw no visible
+// key and are skipped; a row with none left is written as zeros.
+__global__ void __launch_bounds__(256) combine_splits(const __nv_bfloat16* __restrict__ part,
+                                                      const float2* __restrict__ ml,
+                                                      __nv_bfloat16* o, long long o_sb, long long o_sm,
+                                                      long long o_sh, int B, int M, int H, int splits) {
+  // launched as a programmatic dependent of the attention kernel: wait for
+  // that grid to complete and its partials to be visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const long long rows = static_cast<long long>(B) * M * H;
+  const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const long long r = tid >> 3;
+  const int q = static_cast<int>(tid & 7);
+  if (r >= rows) return;
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) {
+    const float2 v = ml[s * rows + r];
+    if (v.y > 0.f) mx = fmaxf(mx, v.x);
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float wsum = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float2 v = ml[s * rows + r];
+    if (!(v.y > 0.f)) continue;
+    const float w = exp2f(v.x - mx) * v.y;
+    wsum += w;
+    const uint4 u = *reinterpret_cast<const uint4*>(part + (s * rows + r) * 64 + q * 8);
+    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[2 * e] += w * __uint_as_float(uw[e] << 16);
+      acc[2 * e + 1] += w * __uint_as_float(uw[e] & 0xffff0000u);
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const long long h = r % H, bm = r / H, m = bm % M, b = bm / M;
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) w[e] = pack_bf16x2(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+  *reinterpret_cast<uint4*>(o + b * o_sb + m * o_sm + h * o_sh + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 int encode_map(CUtensorMap* map, const void* base, int64_t d1, int64_t d2, int64_t d3,
@@ -851,20 +930,75 @@ struct MaskSpec {
   int lengths_dtype = VLAK_I32;
   const void* mask = nullptr;
   int64_t mask_sb = 0, mask_sm = 0;
+  void* workspace = nullptr;  // key-split partials (nullptr: never split)
+  int64_t workspace_bytes = 0;
 };
 
-template <int kMode>
-static cudaError_t launch_mode(const Params& prm, int grid, cudaStream_t cs, int device) {
-  // one-time per (device, mode) opt-in to the large dynamic shared-memory carve-out
+// Query tiling of an item: MT query positions per M-tile, 1 or 2 M-tiles per
+// item, n_mblk query blocks per (b, kv head).
+struct Tiling {
+  int G, MT, tiles, n_mblk, n_chunks;
+};
+static Tiling tiling_of(const vlak_attn_gqa_args* a) {
+  Tiling t;
+  t.G = static_cast<int>(a->H / a->Hkv);
+  const int M = static_cast<int>(a->M);
+  t.MT = std::min(128 / t.G, M);
+  t.tiles = M > t.MT ? 2 : 1;
+  t.n_mblk = (M + t.tiles * t.MT - 1) / (t.tiles * t.MT);
+  t.n_chunks = static_cast<int>((a->N + kChunk - 1) / kChunk);
+  return t;
+}
+
+// Key splits. When the query blocks fill less than half of the CTA slots
+// (small batches, few heads), each block's keys are split into up to
+// n_chunks contiguous ranges processed by separate items, enough to fill the
+// slots; a second kernel merges the splits.
+// Workspace: splits * B * M * H rows of 128 bytes (bf16 O / l), then 8 bytes
+// per row (m, l), the first part rounded up to 256 bytes.
+struct SplitPlan {
+  int splits = 1, split_chunks = 1;
+  int64_t part_bytes = 0, bytes = 0;
+};
+static SplitPlan plan_splits(const vlak_attn_gqa_args* a, const Tiling& t, int sm_count) {
+  SplitPlan sp;
+  sp.split_chunks = std::max(t.n_chunks, 1);
+  const long long base = static_cast<long long>(a->B) * a->Hkv * t.n_mblk;
+  const long long slots = static_cast<long long>(sm_count) * kCtasPerSm;
+  // The merge costs about as much as three chunk steps of one CTA, so a
+  // split must shorten the chain by at least four chunks.
+  if (t.n_chunks < 5 || base <= 0 || 2 * base > slots) return sp;
+  const int want = static_cast<int>(std::min<long long>(t.n_chunks, (slots + base - 1) / base));
+  sp.split_chunks = (t.n_chunks + want - 1) / want;
+  sp.splits = (t.n_chunks + sp.split_chunks - 1) / sp.split_chunks;
+  if (sp.splits < 2) {
+    sp.splits = 1;
+    sp.split_chunks = t.n_chunks;
+    return sp;
+  }
+  const long long rows = static_cast<long long>(a->B) * a->M * a->H;
+  sp.part_bytes = (sp.splits * rows * 128 + 255) / 256 * 256;
+  sp.bytes = sp.part_bytes + sp.splits * rows * 8;
+  return sp;
+}
+
+template <int kMode, bool kSplit>
+static cudaError_t launch_variant(const Params& prm, int grid, cudaStream_t cs, int device) {
+  // one-time per (device, variant) opt-in to the large dynamic shared-memory carve-out
   static std::atomic<int> ready[64];
   if (ready[device].load() == 0) {
-    cudaError_t e = cudaFuncSetAttribute(gqa_attention_sm100<kMode>,
+    cudaError_t e = cudaFuncSetAttribute(gqa_attention_sm100<kMode, kSplit>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     ready[device].store(1);
   }
-  gqa_attention_sm100<kMode><<<grid, kThreads, kSmemBytes, cs>>>(prm);
+  gqa_attention_sm100<kMode, kSplit><<<grid, kThreads, kSmemBytes, cs>>>(prm);
   return cudaGetLastError();
+}
+template <int kMode>
+static cudaError_t launch_mode(const Params& prm, int grid, cudaStream_t cs, int device) {
+  return prm.splits > 1 ? launch_variant<kMode, true>(prm, grid, cs, device)
+                        : launch_variant<kMode, false>(prm, grid, cs, device);
 }
 
 static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSpec& ms = MaskSpec()) {
@@ -918,18 +1052,28 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
 
   Params prm;
   memset(&prm, 0, sizeof(prm));
-  const int G = static_cast<int>(a->H / a->Hkv);
-  const int M = static_cast<int>(a->M);
+  const Tiling tl = tiling_of(a);
+  const int G = tl.G;
   prm.B = static_cast<int>(a->B);
-  prm.M = M;
+  prm.M = static_cast<int>(a->M);
   prm.N = static_cast<int>(a->N);
   prm.H = static_cast<int>(a->H);
   prm.Hkv = static_cast<int>(a->Hkv);
   prm.G = G;
-  prm.MT = std::min(128 / G, M);
-  prm.tiles = M > prm.MT ? 2 : 1;
-  prm.n_mblk = (M + prm.tiles * prm.MT - 1) / (prm.tiles * prm.MT);
-  const long long items = static_cast<long long>(prm.B) * prm.Hkv * prm.n_mblk;
+  prm.MT = tl.MT;
+  prm.tiles = tl.tiles;
+  prm.n_mblk = tl.n_mblk;
+  prm.n_chunks = tl.n_chunks;
+  SplitPlan sp;
+  if (ms.workspace) {
+    if (reinterpret_cast<uintptr_t>(ms.workspace) % 256 != 0)
+      return set_error(VLAK_ERR_ALIGNMENT, "fused_attention_gqa: workspace must be 256-byte aligned");
+    sp = plan_splits(a, tl, dev.sm_count);
+    if (sp.splits > 1 && ms.workspace_bytes < sp.bytes) sp = SplitPlan();  // too small: no split
+  }
+  prm.splits = sp.splits;
+  prm.split_chunks = sp.splits > 1 ? sp.split_chunks : tl.n_chunks;
+  const long long items = static_cast<long long>(prm.B) * prm.Hkv * prm.n_mblk * prm.splits;
   if (items > INT32_MAX) return set_error(VLAK_ERR_INVALID_ARGUMENT, "fused_attention_gqa: too many work items");
   prm.num_items = static_cast<int>(items);
   prm.P = static_cast<int>(P);
@@ -954,6 +1098,14 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
   st = encode_map(&prm.tm_o, a->o, a->H, a->M, a->B, a->o_stride[2], a->o_stride[1],
                   a->o_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "o");
   if (st != VLAK_OK) return st;
+  if (sp.splits > 1) {
+    const int64_t H = a->H;
+    st = encode_map(&prm.tm_part, ms.workspace, H, a->M, a->B * sp.splits, 64, H * 64,
+                    a->M * H * 64, static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT),
+                    "workspace");
+    if (st != VLAK_OK) return st;
+    prm.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(ms.workspace) + sp.part_bytes);
+  }
   st = encode_map(&prm.tm_k, a->k, a->Hkv, a->N, a->B, a->k_stride[2], a->k_stride[1],
                   a->k_stride[0], 1, kChunk, "k");
   if (st != VLAK_OK) return st;
@@ -963,10 +1115,45 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
 
   if (dev.device >= 64) return set_error(VLAK_ERR_CUDA, "device ordinal out of range");
   const int grid = static_cast<int>(std::min<long long>(items, static_cast<long long>(dev.sm_count) * kCtasPerSm));
+
   cudaError_t e = ms.mode == kMaskLength ? launch_mode<kMaskLength>(prm, grid, cs, dev.device)
                   : ms.mode == kMaskBool ? launch_mode<kMaskBool>(prm, grid, cs, dev.device)
                                          : launch_mode<kMaskAnalytic>(prm, grid, cs, dev.device);
   if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa launch failed", e);
+  if (sp.splits > 1) {
+    const long long threads = static_cast<long long>(a->B) * a->M * a->H * 8;
+    // programmatic dependent launch: the merge grid is scheduled while the
+    // attention grid drains and waits on the device for its completion
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = cs;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, combine_splits, static_cast<const __nv_bfloat16*>(ms.workspace),
+                           static_cast<const float2*>(prm.part_ml), o,
+                           static_cast<long long>(a->o_stride[0]),
+                           static_cast<long long>(a->o_stride[1]),
+                           static_cast<long long>(a->o_stride[2]), prm.B, prm.M, prm.H, sp.splits);
+    if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa split combine failed", e);
+  }
+  return VLAK_OK;
+}
+
+static int workspace_size(const vlak_attn_gqa_args* a, int64_t* bytes) {
+  clear_error();
+  if (!bytes) return set_error(VLAK_ERR_INVALID_ARGUMENT, "workspace size: null output");
+  *bytes = 0;
+  int st = validate(a, nullptr, nullptr);
+  if (st != VLAK_OK) return st;
+  if (a->B == 0 || a->M == 0 || a->N == 0) return VLAK_OK;
+  DeviceInfo dev;
+  st = current_device_info(&dev);
+  if (st != VLAK_OK) return st;
+  *bytes = plan_splits(a, tiling_of(a), dev.sm_count).bytes;
   return VLAK_OK;
 }
 
@@ -1035,6 +1222,44 @@ extern "C" int vlak_attn_gqa_masked_fwd(const vlak_attn_gqa_args* args, const vo
   ms.mask = mask;
   ms.mask_sb = mask_stride_b;
   ms.mask_sm = mask_stride_m;
+  return vlak::launch_gqa(args, stream, ms);
+}
+
+extern "C" int vlak_attn_gqa_workspace_size(const vlak_attn_gqa_args* args, int64_t* bytes) {
+  return vlak::workspace_size(args, bytes);
+}
+
+extern "C" int vlak_attn_gqa_fwd_ws(const vlak_attn_gqa_args* args, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
+  vlak::MaskSpec ms;
+  ms.workspace = workspace;
+  ms.workspace_bytes = workspace_bytes;
+  return vlak::launch_gqa(args, stream, ms);
+}
+
+extern "C" int vlak_attn_gqa_varlen_fwd_ws(const vlak_attn_gqa_args* args, const void* lengths,
+                                           int lengths_dtype, void* workspace,
+                                           int64_t workspace_bytes, void* stream) {
+  vlak::MaskSpec ms;
+  ms.mode = vlak::kMaskLength;
+  ms.lengths = lengths;
+  ms.lengths_dtype = lengths_dtype;
+  ms.workspace = workspace;
+  ms.workspace_bytes = workspace_bytes;
+  return vlak::launch_gqa(args, stream, ms);
+}
+
+extern "C" int vlak_attn_gqa_masked_fwd_ws(const vlak_attn_gqa_args* args, const void* mask,
+                                           int64_t mask_stride_b, int64_t mask_stride_m,
+                                           void* workspace, int64_t workspace_bytes,
+                                           void* stream) {
+  vlak::MaskSpec ms;
+  ms.mode = vlak::kMaskBool;
+  ms.mask = mask;
+  ms.mask_sb = mask_stride_b;
+  ms.mask_sm = mask_stride_m;
+  ms.workspace = workspace;
+  ms.workspace_bytes = workspace_bytes;
   return vlak::launch_gqa(args, stream, ms);
 }
 

@@ -89,6 +89,18 @@ vlak_attn_gqa_args gqa_args(const at::Tensor& q, const at::Tensor& k, const at::
   return a;
 }
 
+// Key-split workspace for small batches, from the caching allocator on the
+// current stream (its memory is reused only by work queued after this call
+// on that stream). Undefined when the launch will not split.
+at::Tensor split_workspace(const vlak_attn_gqa_args& a, const at::Tensor& like) {
+  int64_t bytes = 0;
+  check_status(vlak_attn_gqa_workspace_size(&a, &bytes), "fused_attention workspace size");
+  if (bytes == 0) return at::Tensor();
+  return at::empty({bytes}, like.options().dtype(at::kByte));
+}
+void* ws_ptr(const at::Tensor& ws) { return ws.defined() ? ws.data_ptr() : nullptr; }
+int64_t ws_bytes(const at::Tensor& ws) { return ws.defined() ? ws.numel() : 0; }
+
 at::Tensor run_gqa(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
                    int64_t prefix_len, int64_t dead_start, int64_t dead_end, bool v4) {
   const char* op = v4 ? "v4" : "v3";
@@ -103,7 +115,9 @@ at::Tensor run_gqa(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   a.o_stride[1] = o.stride(1);
   a.o_stride[2] = o.stride(2);
   void* stream = c10::cuda::getCurrentCUDAStream().stream();
-  const int st = v4 ? vlak_attn_gqa_v4_fwd(&a, stream) : vlak_attn_gqa_fwd(&a, stream);
+  // v3 and v4 share one kernel; the workspace variant serves both
+  const at::Tensor ws = split_workspace(a, q);
+  const int st = vlak_attn_gqa_fwd_ws(&a, ws_ptr(ws), ws_bytes(ws), stream);
   check_status(st, v4 ? "fused_attention_gqa_v4 launch failed" : "fused_attention_gqa launch failed");
   return o;
 }
@@ -171,13 +185,13 @@ at::Tensor fused_attention(const at::Tensor& q_in, const at::Tensor& k_in, const
     a.scale = scale;
     a.prefix_len = -1;
     int status;
-    if (prefix_len >= 0) {
-      a.prefix_len = std::min(prefix_len, N);  // a prefix past N makes every key visible
-      status = vlak_attn_gqa_fwd(&a, stream);
-    } else if (mask.defined()) {
-      status = vlak_attn_gqa_masked_fwd(&a, mask.data_ptr(), M * N, N, stream);
+    if (prefix_len >= 0) a.prefix_len = std::min(prefix_len, N);  // a prefix past N shows every key
+    const at::Tensor ws = split_workspace(a, q);
+    if (mask.defined() && prefix_len < 0) {
+      status = vlak_attn_gqa_masked_fwd_ws(&a, mask.data_ptr(), M * N, N, ws_ptr(ws), ws_bytes(ws),
+                                           stream);
     } else {
-      status = vlak_attn_gqa_fwd(&a, stream);
+      status = vlak_attn_gqa_fwd_ws(&a, ws_ptr(ws), ws_bytes(ws), stream);
     }
     check_status(status, "fused_attention launch failed");
     return o;
@@ -209,9 +223,10 @@ at::Tensor fused_attention_gqa_varlen(const at::Tensor& q, const at::Tensor& k,
   a.o_stride[0] = o.stride(0);
   a.o_stride[1] = o.stride(1);
   a.o_stride[2] = o.stride(2);
-  const int st = vlak_attn_gqa_varlen_fwd(
-      &a, lengths.data_ptr(), lengths.scalar_type() == at::kLong ? VLAK_I64 : VLAK_I32,
-      c10::cuda::getCurrentCUDAStream().stream());
+  const at::Tensor ws = split_workspace(a, q);
+  const int st = vlak_attn_gqa_varlen_fwd_ws(
+      &a, lengths.data_ptr(), lengths.scalar_type() == at::kLong ? VLAK_I64 : VLAK_I32, ws_ptr(ws),
+      ws_bytes(ws), c10::cuda::getCurrentCUDAStream().stream());
   check_status(st, "fused_attention_gqa_varlen launch failed");
   return o;
 }
