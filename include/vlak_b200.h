@@ -184,6 +184,24 @@ VLAK_API int vlak_attn_gqa_masked_fwd_ws(const vlak_attn_gqa_args* args, const v
                                          void* workspace, int64_t workspace_bytes,
                                          void* stream);
 
+/* vlak_attn_gqa_fwd that allocates nothing. No counterpart in the reference.
+ * For callers that must not allocate device memory per call: a control loop
+ * that reserves all of its memory at start-up (cudaMalloc synchronizes the
+ * device and can stall the loop for milliseconds), or a host calling through
+ * a C FFI without a pool allocator to hand out a workspace. Small batches
+ * still split their keys across CTAs; the split scratch is a static 8 MiB
+ * device buffer of this library, one per device.
+ *  - The first call on a device looks up that buffer's address
+ *    (cudaGetSymbolAddress); make the first call before any stream capture.
+ *  - A problem whose split scratch would exceed 8 MiB (see
+ *    vlak_attn_gqa_workspace_size) is rejected with VLAK_ERR_INVALID_ARGUMENT;
+ *    use vlak_attn_gqa_fwd_ws for it.
+ *  - Every call on a device shares the buffer: calls whose GPU work overlaps
+ *    (different streams) race on it and corrupt each other's results; keep
+ *    them ordered on one stream. No part of it has to start at zero: a call
+ *    writes every entry its merge reads. */
+VLAK_API int vlak_attn_gqa_fwd_noalloc(const vlak_attn_gqa_args* args, void* stream);
+
 /* Non-GQA attention on the CUDA cores with fp32 math: the v1 path of
  * vlak::fused_attention for fp32 / fp16 / fp64 inputs (replaces
  * fused_attention_warp_row and its host branch,

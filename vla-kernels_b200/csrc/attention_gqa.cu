@@ -56,6 +56,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <mutex>
 
 #include "vlak_device.cuh"
 #include "vlak_internal.h"
@@ -1261,6 +1262,64 @@ extern "C" int vlak_attn_gqa_masked_fwd_ws(const vlak_attn_gqa_args* args, const
   ms.workspace = workspace;
   ms.workspace_bytes = workspace_bytes;
   return vlak::launch_gqa(args, stream, ms);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free GQA attention. For callers that must not allocate device
+// memory per call: a robot-control loop that reserves all of its memory at
+// start-up and treats an allocation inside the loop as a latency fault
+// (cudaMalloc synchronizes the device and can take milliseconds), or a host
+// reaching the library through a C FFI (Go, Java, plain C) that has no pool
+// allocator to draw a workspace from. The key-split scratch then comes from
+// this file's static device buffer instead of a caller workspace.
+namespace vlak {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = int64_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the static scratch on the current device, looked up once
+// per device (with that device current) on its first call.
+int noalloc_scratch(void** out) {
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static void* addr[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error("cudaGetDevice", e);
+  if (dev < 0 || dev >= kMaxDev) return set_error(VLAK_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error("fused_attention_gqa_noalloc: scratch address", e);
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return VLAK_OK;
+}
+
+}  // namespace
+}  // namespace vlak
+
+extern "C" int vlak_attn_gqa_fwd_noalloc(const vlak_attn_gqa_args* args, void* stream) {
+  using namespace vlak;
+  int64_t need = 0;
+  int st = workspace_size(args, &need);  // validates the arguments too
+  if (st != VLAK_OK) return st;
+  if (need > kNoAllocScratchBytes)
+    return set_errorf(VLAK_ERR_INVALID_ARGUMENT,
+                      "fused_attention_gqa_noalloc: this problem needs %lld bytes of key-split "
+                      "scratch, more than the %lld-byte static buffer; call vlak_attn_gqa_fwd_ws "
+                      "with a workspace instead",
+                      static_cast<long long>(need), static_cast<long long>(kNoAllocScratchBytes));
+  MaskSpec ms;
+  if (need > 0) {
+    st = noalloc_scratch(&ms.workspace);
+    if (st != VLAK_OK) return st;
+    ms.workspace_bytes = kNoAllocScratchBytes;
+  }
+  return launch_gqa(args, stream, ms);
 }
 
 extern "C" int vlak_device_error_read(int* code) {
