@@ -194,11 +194,27 @@ template <> struct Pair2<__nv_bfloat16> {
   }
 };
 
+// exp values of a row in (0, 1] held as f16 pairs (11 significant bits; below
+// 2^-14 an absolute error under 2^-25), between the sum and the output pass
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ void unpack_f16x2(uint32_t u, float& lo, float& hi) {
+  asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
+      : "=f"(lo), "=f"(hi) : "r"(u));
+}
+
 // Register-resident row for 2-byte element types: the row stays in registers
 // as the raw 16-byte vectors (4 registers per 8 elements, half the footprint
 // of fp32 copies), so a 32768-column row fits 512 threads x 8 vectors at
 // under 64 registers and two rows share an SM. The max runs on packed pairs;
-// exp is evaluated once for the sum and again for the output.
+// the sum pass evaluates each exp once and keeps it in the same registers as
+// an f16 pair, so the output pass only scales by 1 / sum: one MUFU operation
+// per element, which is what bounds wide rows at full HBM rate. The outputs
+// are the f16-rounded exps times the fp32 reciprocal, rounded to the output
+// type (within 2^-11 + one output ulp relative).
 template <typename T, int RV, int NT, class Group>
 __device__ __forceinline__ void row_softmax_reg_packed(const T* __restrict__ xr,
                                                        T* __restrict__ yr, int n, int t,
@@ -238,8 +254,14 @@ __device__ __forceinline__ void row_softmax_reg_packed(const T* __restrict__ xr,
     if (t + i * NT < sg.nvec) {
       float f[V];
       E::unpack(raw[i], f);
+      uint32_t w[4];
 #pragma unroll
-      for (int j = 0; j < V; ++j) s += exp_shift<T>(f[j], m);
+      for (int k = 0; k < 4; ++k) {
+        const float e0 = exp_shift<T>(f[2 * k], m), e1 = exp_shift<T>(f[2 * k + 1], m);
+        s += e0 + e1;
+        w[k] = pack_f16x2(e0, e1);
+      }
+      raw[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
   if (t < sg.head) { hv = exp_shift<T>(hv, m); s += hv; }
@@ -252,10 +274,14 @@ __device__ __forceinline__ void row_softmax_reg_packed(const T* __restrict__ xr,
   for (int i = 0; i < RV; ++i) {
     const int vi = t + i * NT;
     if (vi < sg.nvec) {
+      const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
       float f[V];
-      E::unpack(raw[i], f);
 #pragma unroll
-      for (int j = 0; j < V; ++j) f[j] = exp_shift<T>(f[j], m) * inv;
+      for (int k = 0; k < 4; ++k) {
+        unpack_f16x2(w[k], f[2 * k], f[2 * k + 1]);
+        f[2 * k] *= inv;
+        f[2 * k + 1] *= inv;
+      }
       st_stream16(yb + static_cast<size_t>(vi) * 16, E::pack(f));
     }
   }
