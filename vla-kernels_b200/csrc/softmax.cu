@@ -143,13 +143,34 @@ __device__ __forceinline__ void row_softmax_reg(const T* __restrict__ xr, T* __r
   m = grp.max(m);
 
   float s = 0.f;
+  if constexpr (sizeof(T) == 2) {
+    // element pairs through the f32x2 FMA pipe: exp2(x log2e - m log2e); an
+    // all -inf row gives NaN (as torch), a -inf element 0
+    const float nb = -m * kLog2e;
+    const uint64_t sc2 = f2_pack(kLog2e, kLog2e), nb2 = f2_pack(nb, nb);
+    uint64_t s2 = f2_pack(0.f, 0.f);
 #pragma unroll
-  for (int i = 0; i < RV; ++i)
+    for (int i = 0; i < RV; ++i)
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      v[i][j] = exp_shift<T>(v[i][j], m);
-      s += v[i][j];
-    }
+      for (int j = 0; j < V; j += 2) {
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(v[i][j], v[i][j + 1]), sc2, nb2), x0, x1);
+        v[i][j] = ex2(x0);
+        v[i][j + 1] = ex2(x1);
+        s2 = f2_add(s2, f2_pack(v[i][j], v[i][j + 1]));
+      }
+    float s0, s1;
+    f2_unpack(s2, s0, s1);
+    s = s0 + s1;
+  } else {
+#pragma unroll
+    for (int i = 0; i < RV; ++i)
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        v[i][j] = exp_shift<T>(v[i][j], m);
+        s += v[i][j];
+      }
+  }
   if (t < sg.head) { hv = exp_shift<T>(hv, m); s += hv; }
   if (t < sg.tail) { tv = exp_shift<T>(tv, m); s += tv; }
   s = grp.sum(s);
@@ -161,8 +182,15 @@ __device__ __forceinline__ void row_softmax_reg(const T* __restrict__ xr, T* __r
     const int vi = t + i * NT;
     if (vi < sg.nvec) {
       float o[V];
+      if constexpr (sizeof(T) == 2) {
+        const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
-      for (int j = 0; j < V; ++j) o[j] = normalize<T>(v[i][j], s, inv);
+        for (int j = 0; j < V; j += 2)
+          f2_unpack(f2_mul(f2_pack(v[i][j], v[i][j + 1]), inv2), o[j], o[j + 1]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) o[j] = normalize<T>(v[i][j], s, inv);
+      }
       st_stream16(yb + static_cast<size_t>(vi) * 16, E::pack(o));
     }
   }
