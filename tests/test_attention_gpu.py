@@ -246,6 +246,16 @@ def test_cuda_graph_capture_replays():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
+    # B = 8 runs the key-split form: the captured workspace and merge must
+    # serve new inputs on replay
+    for seed in (5, 6):
+        g2 = torch.Generator(device="cuda").manual_seed(seed)
+        q.copy_(rand(8, 50, 15, 64, gen=g2))
+        k.copy_(rand(8, 291, 5, 64, gen=g2))
+        v.copy_(rand(8, 291, 5, 64, gen=g2))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, fused_attention_gqa(q, k, v, prefix_len=241))
 
 
 def test_stress_randomized():
