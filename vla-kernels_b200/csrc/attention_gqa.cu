@@ -117,10 +117,22 @@ constexpr int kWaitSoftmax = 1;  // softmax warps: S ready
 // shared memory): the two CTAs' chunk pipelines are independent, so one
 // CTA's softmax warps compute while the other's wait on TMEM loads, barrier
 // hand-offs or the tensor pipe.
-constexpr int kThreads = 320;   // 10 warps
+constexpr int kThreads = 320;   // 10 warps (the narrow layout below: 7)
 constexpr int kCtasPerSm = 2;
 constexpr int kSoftmaxWarps = 8;  // 4 per M-tile, one per TMEM lane quarter
 constexpr int kWarpProducer = 8, kWarpMma = 9;
+// Warp layout. The full one gives each M-tile four softmax warps. The narrow
+// one serves problems whose second M-tile never holds more than 32 rows (one
+// query block, e.g. the expert self-attention: 8 positions x 3 heads = 24
+// rows in TMEM lanes 0-31): one warp covers that tile, and with 7 warps per
+// CTA the register cap of two CTAs per SM rises from 96 to 144.
+template <bool kNarrow> struct WarpLayout {
+  static constexpr int kThreads = kNarrow ? 224 : 320;
+  static constexpr int kSoftmaxWarps = kNarrow ? 5 : 8;
+  static constexpr int kWarpProducer = kNarrow ? 5 : 8;
+  static constexpr int kWarpMma = kNarrow ? 6 : 9;
+  static constexpr int kTile1Warps = kNarrow ? 1 : 4;
+};
 // Key pairs whose exp2 runs on the FMA pipe instead of MUFU: bit (k % 8) of
 // the mask selects pair k of a 32-key group (full groups only). With two CTAs
 // per SM the MUFU pipe runs at about a fifth of its rate, so all pairs use it
@@ -291,9 +303,10 @@ __device__ __forceinline__ int chunk_cols(const Params& p, int c) {
   return (width + 15) & ~15;  // MMA N must be a multiple of 16
 }
 
-template <int kMode, bool kSplit>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+template <int kMode, bool kSplit, bool kNarrow>
+__global__ void __launch_bounds__(WarpLayout<kNarrow>::kThreads, kCtasPerSm)
 gqa_attention_sm100(const __grid_constant__ Params p) {
+  using WL = WarpLayout<kNarrow>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte-swizzled operand tiles; the barrier
   // block sits in the alignment gap when it fits there
@@ -315,9 +328,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       // one arrival per M-tile once its O has been read out of the buffer
       // (tile 0 arrives twice for a one-tile item)
       mbar_init(&bars->q_empty[i], 2);
-      mbar_init(&bars->o_staged[i], 4);  // one arrival per softmax warp of the tile
+      mbar_init(&bars->o_staged[i], i == 0 ? 4 : WL::kTile1Warps);  // one arrival per softmax warp of the tile
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp of the tile
+      mbar_init(&bars->p_full[i], i == 0 ? 4 : WL::kTile1Warps);  // one arrival per softmax warp of the tile
       mbar_init(&bars->pv_done[i], 1);
       mbar_init(&bars->o_full[i], 1);
     }
@@ -329,13 +342,13 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kWarpMma) {
+  if (warp == WL::kWarpMma) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
   // Q rows that no TMA box covers feed only discarded rows; clear them once so
   // they hold finite values.
-  for (int i = threadIdx.x; i < 2 * kQBytes / 16; i += kThreads)
+  for (int i = threadIdx.x; i < 2 * kQBytes / 16; i += WL::kThreads)
     reinterpret_cast<uint4*>(q_smem)[i] = make_uint4(0, 0, 0, 0);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   tc_fence_before();
@@ -346,7 +359,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   // on; it waits for this grid's completion before reading anything
   if (kSplit) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  if (warp == kWarpProducer) {
+  if (warp == WL::kWarpProducer) {
     // ------------------------------------------------------------ producer
     // The whole warp runs this loop (converged); one elected lane issues.
     if (lane == 0) {
@@ -403,7 +416,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     for (int s = 0; s < kStages; ++s)
       if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
     __syncwarp();
-  } else if (warp == kWarpMma) {
+  } else if (warp == WL::kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     // Per item and chunk j of tile t: S_t(j) = Q_t K(j)^T into the tile's S
     // columns; once softmax has written P_t(j) over them, O_t (+)= P_t(j) V(j)
@@ -502,7 +515,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       bounded_wait(&bars->drain, 0, abort_flag, false);
     }
     __syncwarp();  // reconverge before the CTA-wide barrier and the dealloc
-  } else if (warp < kSoftmaxWarps) {
+  } else if (warp < WL::kSoftmaxWarps) {
     // ------------------------------------------------------------ softmax
     // Warp w owns TMEM lane quarter w % 4 (32 query rows) of M-tile w / 4.
     // A chunk's 64 keys are handled as two 32-key groups: load, max, exp,
@@ -796,7 +809,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) {
+  if (warp == WL::kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -983,23 +996,31 @@ static SplitPlan plan_splits(const vlak_attn_gqa_args* a, const Tiling& t, int s
   return sp;
 }
 
-template <int kMode, bool kSplit>
+template <int kMode, bool kSplit, bool kNarrow>
 static cudaError_t launch_variant(const Params& prm, int grid, cudaStream_t cs, int device) {
   // one-time per (device, variant) opt-in to the large dynamic shared-memory carve-out
   static std::atomic<int> ready[64];
   if (ready[device].load() == 0) {
-    cudaError_t e = cudaFuncSetAttribute(gqa_attention_sm100<kMode, kSplit>,
+    cudaError_t e = cudaFuncSetAttribute(gqa_attention_sm100<kMode, kSplit, kNarrow>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     ready[device].store(1);
   }
-  gqa_attention_sm100<kMode, kSplit><<<grid, kThreads, kSmemBytes, cs>>>(prm);
+  gqa_attention_sm100<kMode, kSplit, kNarrow>
+      <<<grid, WarpLayout<kNarrow>::kThreads, kSmemBytes, cs>>>(prm);
   return cudaGetLastError();
 }
 template <int kMode>
 static cudaError_t launch_mode(const Params& prm, int grid, cudaStream_t cs, int device) {
-  return prm.splits > 1 ? launch_variant<kMode, true>(prm, grid, cs, device)
-                        : launch_variant<kMode, false>(prm, grid, cs, device);
+  // the narrow warp layout when the second M-tile holds at most 32 rows
+  // (analytic mask only: the sites of the other modes never qualify)
+  if constexpr (kMode == kMaskAnalytic) {
+    if (prm.tiles == 2 && prm.n_mblk == 1 && (prm.M - prm.MT) * prm.G <= 32)
+      return prm.splits > 1 ? launch_variant<kMode, true, true>(prm, grid, cs, device)
+                            : launch_variant<kMode, false, true>(prm, grid, cs, device);
+  }
+  return prm.splits > 1 ? launch_variant<kMode, true, false>(prm, grid, cs, device)
+                        : launch_variant<kMode, false, false>(prm, grid, cs, device);
 }
 
 static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSpec& ms = MaskSpec()) {
