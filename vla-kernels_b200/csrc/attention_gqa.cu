@@ -599,6 +599,14 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           const int c0 = c * kChunk;
           const int ncols = chunk_cols(p, c);
           float alpha_o = 1.f, alpha_p = 1.f;  // this chunk's rescale factors (O, first group's P)
+          // The narrow layout has the registers to load both groups' scores
+          // at once (one TMEM round trip per chunk instead of two).
+          float sv2[kNarrow ? kChunk / 32 : 1][32];
+          if constexpr (kNarrow) {
+            tmem_ld32(tS, sv2[0]);
+            tmem_ld32(tS + 32, sv2[1]);
+            tmem_wait_ld();
+          }
 #pragma unroll
           for (int gq = 0; gq < kChunk / 32; ++gq) {
             const int g0 = c0 + 32 * gq;
@@ -625,11 +633,13 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
             const bool none = __all_sync(kFullMask, none_l);
             if (kMode != kMaskBool && !full && !none)
               vm = valid ? (low(rds - g0) | (low(e2 - g0) & ~low(rde - g0))) : 0u;
-            float sv[32];
+            float (&sv)[32] = sv2[kNarrow ? gq : 0];
             float mx = -INFINITY;
             if (!none) {
-              tmem_ld32(tS + 32 * gq, sv);
-              tmem_wait_ld();
+              if constexpr (!kNarrow) {
+                tmem_ld32(tS + 32 * gq, sv);
+                tmem_wait_ld();
+              }
               // group max with four independent accumulators
               float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
               if (full) {
