@@ -126,13 +126,21 @@ constexpr int kWarpProducer = 8, kWarpMma = 9;
 // query block, e.g. the expert self-attention: 8 positions x 3 heads = 24
 // rows in TMEM lanes 0-31): one warp covers that tile, and with 7 warps per
 // CTA the register cap of two CTAs per SM rises from 96 to 144.
+// In the narrow layout the second tile's rows go to TMEM lane quarter 2 in
+// one of an SM's two CTAs and quarter 3 in the other (the CTAs own TMEM
+// columns [0, 256) and [256, 512)), served by warp 6 or 7: no SM
+// sub-partition then runs more than three softmax warps. The other of
+// warps 6 / 7 has no role.
 template <bool kNarrow> struct WarpLayout {
-  static constexpr int kThreads = kNarrow ? 224 : 320;
-  static constexpr int kSoftmaxWarps = kNarrow ? 5 : 8;
-  static constexpr int kWarpProducer = kNarrow ? 5 : 8;
-  static constexpr int kWarpMma = kNarrow ? 6 : 9;
+  static constexpr int kThreads = kNarrow ? 256 : 320;
+  static constexpr int kWarpProducer = kNarrow ? 4 : 8;
+  static constexpr int kWarpMma = kNarrow ? 5 : 9;
   static constexpr int kTile1Warps = kNarrow ? 1 : 4;
 };
+// first TMEM lane (= row of the tile) of the narrow second tile
+__device__ __forceinline__ int narrow_tile1_row0(uint32_t tmem) {
+  return 64 + 32 * static_cast<int>((tmem >> 8) & 1u);
+}
 // Key pairs whose exp2 runs on the FMA pipe instead of MUFU: bit (k % 8) of
 // the mask selects pair k of a 32-key group (full groups only). With two CTAs
 // per SM the MUFU pipe runs at about a fifth of its rate, so all pairs use it
@@ -176,6 +184,8 @@ struct __align__(64) Params {
   CUtensorMap tm_k;  // dims (64, Hkv, N, B), box (64, 1, 64, 1)
   CUtensorMap tm_v;
   CUtensorMap tm_o;  // dims (64, H, M, B), box (64, G, MT, 1), TMA stores of O
+  // narrow layout: the second M-tile's M - MT positions (box (64, G, M - MT, 1))
+  CUtensorMap tm_q1, tm_o1;
   // Key splits (splits > 1): split s of a query block covers chunks
   // [s * split_chunks, (s + 1) * split_chunks) and writes O / l in bf16 to the
   // partials (dims (64, H, M, splits * B), box as tm_o) and (reference max,
@@ -359,6 +369,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
   // on; it waits for this grid's completion before reading anything
   if (kSplit) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+  const int t1_row0 = kNarrow ? narrow_tile1_row0(tmem) : 0;  // narrow: row offset of tile 1
+  const bool softmax_warp = kNarrow ? (warp < 4 || warp == 4 + t1_row0 / 32) : (warp < 8);
   if (warp == WL::kWarpProducer) {
     // ------------------------------------------------------------ producer
     // The whole warp runs this loop (converged); one elected lane issues.
@@ -385,12 +397,21 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         ok = false;
         break;
       }
-      const uint32_t qbytes = static_cast<uint32_t>(it.tiles_active * p.G * p.MT * kRowBytes);
+      const uint32_t qbytes = static_cast<uint32_t>(
+          (kNarrow ? p.G * p.MT + (it.tiles_active - 1) * p.G * (p.M - p.MT)
+                   : it.tiles_active * p.G * p.MT) * kRowBytes);
       mbar_arrive_expect_tx_elect(&bars->q_full[qb], qbytes);
       ++q_armed;
-      for (int t = 0; t < it.tiles_active; ++t)
-        tma_load_4d_elect(q_smem + qb * kQBytes + t * kTileBytes, &p.tm_q, &bars->q_full[qb], 0,
-                          it.kvh * p.G, it.m0 + t * p.MT, it.b);
+      tma_load_4d_elect(q_smem + qb * kQBytes, &p.tm_q, &bars->q_full[qb], 0, it.kvh * p.G, it.m0,
+                        it.b);
+      if (it.tiles_active == 2) {
+        if (kNarrow)
+          tma_load_4d_elect(q_smem + qb * kQBytes + kTileBytes + t1_row0 * kRowBytes, &p.tm_q1,
+                            &bars->q_full[qb], 0, it.kvh * p.G, it.m0 + p.MT, it.b);
+        else
+          tma_load_4d_elect(q_smem + qb * kQBytes + kTileBytes, &p.tm_q, &bars->q_full[qb], 0,
+                            it.kvh * p.G, it.m0 + p.MT, it.b);
+      }
       for (int c = first_live<kMode, kSplit>(p, it); c >= 0; c = next_live<kMode, kSplit>(p, it, c + 1)) {
         const int s = kv % kStages;
         if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
@@ -515,19 +536,25 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       bounded_wait(&bars->drain, 0, abort_flag, false);
     }
     __syncwarp();  // reconverge before the CTA-wide barrier and the dealloc
-  } else if (warp < WL::kSoftmaxWarps) {
+  } else if (softmax_warp) {
     // ------------------------------------------------------------ softmax
     // Warp w owns TMEM lane quarter w % 4 (32 query rows) of M-tile w / 4.
     // A chunk's 64 keys are handled as two 32-key groups: load, max, exp,
     // P store per group, so a thread holds 32 scores at a time.
-    const int t = warp >> 2;
+    const int t = warp < 4 ? 0 : 1;
     const int quarter = warp & 3;
+    // the warp that stores the tile's O and hands its Q buffer back: quarter
+    // 0, or the narrow second tile's only warp
+    const bool leader = quarter == 0 || (kNarrow && t == 1);
     const int row = quarter * 32 + lane;    // TMEM lane = row within the tile
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + t * kTileCols;
     const uint32_t tS = tbase + kColS;      // S; P (bf16 pairs) over its first 32 columns
     const uint32_t tO = tbase + kColO;
-    const int m_local = row / p.G;
-    const int g = row - m_local * p.G;
+    // the tile's rows start at TMEM lane 0, or at t1_row0 for the narrow
+    // second tile
+    const int row_rel = row - (t == 1 ? t1_row0 : 0);
+    const int m_local = row_rel >= 0 ? row_rel / p.G : p.MT;  // p.MT: no row here
+    const int g = row_rel >= 0 ? row_rel - m_local * p.G : 0;
     uint32_t sph = 0, oph = 0, pv_seen = 0;  // pv_seen: this tile's P.V products so far
     uint32_t qi = 0;    // items with live chunks so far; item qi uses Q buffer qi & 1
     // Quarter-0 warps: the Q buffer whose staged O rows this tile's last TMA
@@ -555,8 +582,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       const int m = m_first + m_local;
       const bool valid = (m_local < p.MT) && (m < p.M);
       // a warp whose rows are all invalid skips the arithmetic
-      const int warp_first_m = m_first + (quarter * 32) / p.G;
-      const bool warp_active = ((quarter * 32) / p.G < p.MT) && (warp_first_m < p.M);
+      const bool warp_active = __any_sync(kFullMask, valid);
       // this row's visible set [0, ds) U [de, e2) (mask modes 0 and 1) or its
       // bool-mask row (mode 2)
       const int rds = kMode == kMaskAnalytic ? p.ds : 0;
@@ -794,14 +820,17 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       if (kSplit && valid) p.part_ml[part_row()] = make_float2(m_run, l_run);
       fence_proxy_async_smem();
       mbar_arrive_elect(&bars->o_staged[t], 1u);
-      if (quarter == 0) {
+      if (leader) {
         // o_staged completes one phase per item of the tile, like o_full
         if (!__all_sync(kFullMask, bounded_wait(&bars->o_staged[t], oph ^ 1u, abort_flag))) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          if (kSplit)
+          if (kNarrow && t == 1)  // the tile's rows start at t1_row0
+            tma_store_4d(&p.tm_o1, stage + t1_row0 * kRowBytes, 0, it.kvh * p.G, m_first,
+                         kSplit ? it.split * p.B + it.b : it.b);
+          else if (kSplit)
             tma_store_4d(&p.tm_part, stage, 0, it.kvh * p.G, m_first, it.split * p.B + it.b);
           else
             tma_store_4d(&p.tm_o, stage, 0, it.kvh * p.G, m_first, it.b);
@@ -814,7 +843,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       tc_fence_before();
     }
     // the TMA stores of this warp's last items complete before the CTA exits
-    if (quarter == 0 && lane == 0) bulk_wait_all0();
+    if (leader && lane == 0) bulk_wait_all0();
   }
 
   tc_fence_before();
@@ -1130,6 +1159,22 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
   st = encode_map(&prm.tm_o, a->o, a->H, a->M, a->B, a->o_stride[2], a->o_stride[1],
                   a->o_stride[0], static_cast<uint32_t>(G), static_cast<uint32_t>(prm.MT), "o");
   if (st != VLAK_OK) return st;
+  // narrow layout: one query block whose second M-tile holds <= 32 rows
+  const bool narrow = ms.mode == kMaskAnalytic && prm.tiles == 2 && prm.n_mblk == 1 &&
+                      (prm.M - prm.MT) * G <= 32;
+  if (narrow) {
+    const uint32_t n1 = static_cast<uint32_t>(prm.M - prm.MT);
+    st = encode_map(&prm.tm_q1, a->q, a->H, a->M, a->B, a->q_stride[2], a->q_stride[1],
+                    a->q_stride[0], static_cast<uint32_t>(G), n1, "q");
+    if (st != VLAK_OK) return st;
+    if (ms.workspace && sp.splits > 1)
+      st = encode_map(&prm.tm_o1, ms.workspace, a->H, a->M, a->B * sp.splits, 64, a->H * 64,
+                      a->M * a->H * 64, static_cast<uint32_t>(G), n1, "workspace");
+    else
+      st = encode_map(&prm.tm_o1, a->o, a->H, a->M, a->B, a->o_stride[2], a->o_stride[1],
+                      a->o_stride[0], static_cast<uint32_t>(G), n1, "o");
+    if (st != VLAK_OK) return st;
+  }
   if (sp.splits > 1) {
     const int64_t H = a->H;
     st = encode_map(&prm.tm_part, ms.workspace, H, a->M, a->B * sp.splits, 64, H * 64,
