@@ -113,14 +113,11 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
 constexpr int kWaitMma = 1;      // MMA warp: P ready, K/V ready
 constexpr int kWaitSoftmax = 1;  // softmax warps: S ready
 
-// Two CTAs share each SM (each 10 warps, 256 TMEM columns, under 100 KB of
-// shared memory): the two CTAs' chunk pipelines are independent, so one
-// CTA's softmax warps compute while the other's wait on TMEM loads, barrier
-// hand-offs or the tensor pipe.
-constexpr int kThreads = 320;   // 10 warps (the narrow layout below: 7)
+// Two CTAs share each SM (each 10 warps, or 8 in the narrow layout below; 256
+// TMEM columns; 113 KB of shared memory): the two CTAs' chunk pipelines are
+// independent, so one CTA's softmax warps compute while the other's wait on
+// TMEM loads, barrier hand-offs or the tensor pipe.
 constexpr int kCtasPerSm = 2;
-constexpr int kSoftmaxWarps = 8;  // 4 per M-tile, one per TMEM lane quarter
-constexpr int kWarpProducer = 8, kWarpMma = 9;
 // Warp layout. The full one gives each M-tile four softmax warps. The narrow
 // one serves problems whose second M-tile never holds more than 32 rows (one
 // query block, e.g. the expert self-attention: 8 positions x 3 heads = 24
