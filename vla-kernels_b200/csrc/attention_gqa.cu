@@ -25,6 +25,11 @@
 //   warp 9      TMEM allocator and MMA issuer (one elected lane):
 //               S_t = Q_t K_c^T  (SS MMA, M=128, N=chunk width, K=64)
 //               O_t (+)= P_t V_c (TS MMA: P from TMEM, V from smem, N=64)
+// Narrow layout (8 warps, 128 registers), when M-tile 1 never holds more than
+// 32 rows (one query block; the expert self-attention's 8 positions x 3
+// heads): warps 0-3 softmax for M-tile 0, warp 4 producer, warp 5 MMA issuer,
+// and warp 6 or 7 softmax for M-tile 1, whose rows are loaded with a small
+// TMA box into TMEM lane quarter 2 or 3 (one per CTA of an SM).
 // Keys are processed in 64-key chunks. Softmax writes P over the columns of S
 // it has read; the MMA warp then issues P.V and, behind it in issue order,
 // the next chunk's S into the same columns.
