@@ -134,6 +134,25 @@ def test_c5_batch_2048_properties():
     check(a[idx.cuda()], oracle(q[idx.cuda()], k[idx.cuda()], v[idx.cuda()], s.P, 0, 0))
 
 
+# Shapes with one query block whose second M-tile holds at most 32 rows (the
+# kernel's narrow warp layout), over several GQA ratios, masks and batches
+# (the small batches also take the key-split path):
+# (B, M, N, H, Hkv, P, ds, de)
+NARROW = [
+    (2, 150, 300, 4, 4, 250, 0, 0),      # G=1: 22 rows in tile 1
+    (1, 70, 200, 8, 4, 150, 20, 60),     # G=2: 12 rows
+    (3, 38, 100, 16, 4, 100, 0, 0),      # G=4: 24 rows
+    (1, 19, 77, 8, 1, 50, 10, 20),       # G=8: 24 rows
+    (2, 30, 64, 5, 1, 64, 0, 0),         # G=5: 25 rows
+    (96, 50, 291, 15, 5, 241, 196, 240),  # C3 with the real dead band, unsplit
+]
+
+
+@pytest.mark.parametrize("case", NARROW)
+def test_narrow_layout_shapes(case):
+    run(fused_attention_gqa, *case, seed=12)
+
+
 def test_strided_inputs():
     # tests/test_attention_gqa.py:66-74
     g = torch.Generator(device="cuda").manual_seed(1)
