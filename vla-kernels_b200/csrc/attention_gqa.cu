@@ -515,6 +515,10 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           if (nxt >= 0) {
             if (!wait_kv(j + 1)) { ok = false; break; }
             issue_s(0, nxt, j + 1);
+          } else {
+            // tile 0's O is final once its last P.V completes: its epilogue
+            // need not wait for tile 1's last P
+            umma_commit_elect(&bars->o_full[0]);
           }
           if (two) {
             if (!wait_p(1)) { ok = false; break; }
@@ -526,9 +530,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           ++j;
         }
         if (!ok) break;
-        // one o_full phase per item with live chunks; each follows the
-        // softmax warps' arrivals on p_full, so no phase can run ahead of them
-        umma_commit_elect(&bars->o_full[0]);
+        // one o_full phase per item with live chunks and tile; each follows
+        // the softmax warps' arrivals on p_full, so no phase can run ahead
         umma_commit_elect(&bars->o_full[1], two ? 1u : 0u);
         kv += j;
         ++qi;
