@@ -65,6 +65,23 @@ def test_workspace_size_follows_occupancy():
     assert capi.workspace_size(*big, prefix_len=241) == 0  # 320 blocks fill the GPU unsplit
 
 
+def splits_of(case):
+    """Number of key splits the library plans for a CASES entry (from the
+    workspace size: 128 bytes of partial O and 8 of (m, l) per row and split)."""
+    B, M, N, H, Hkv, P, ds, de = case
+    q, k, v = inputs(B, M, N, H, Hkv, 0)
+    return round(capi.workspace_size(q, k, v, prefix_len=P, dead_start=ds, dead_end=de) / (B * M * H * 136))
+
+
+def test_cases_reach_both_merge_forms():
+    # combine_splits loads up to 8 splits in one batch and loops over batches
+    # of 8 beyond that: CASES holds both kinds
+    counts = [splits_of(c) for c in CASES]
+    assert any(2 <= n <= 8 for n in counts), counts
+    assert any(n > 8 for n in counts), counts
+    assert splits_of(CASES[0]) == 5  # C3 at B = 1: 5 chunks, one per split
+
+
 def test_missing_or_small_workspace_runs_unsplit():
     q, k, v = inputs(1, 50, 291, 15, 5, 5)
     st, o_plain = capi.attn_gqa_plain(q, k, v, prefix_len=241)

@@ -222,7 +222,11 @@ constexpr int kMaskAnalytic = 0, kMaskLength = 1, kMaskBool = 2;
 
 struct Barriers {
   uint64_t q_full[2], q_empty[2];  // [Q buffer]
-  uint64_t kv_full[kStages], kv_empty[kStages];
+  // K (and V) of a stage landed. The split kernel, whose items are a few
+  // chunks long, gives V its own barrier so that an item's first S product
+  // waits for K alone; in the unsplit kernel both land on k_full (one probe
+  // fewer per chunk on the MMA warp's chain).
+  uint64_t k_full[kStages], v_full[kStages], kv_empty[kStages];
   uint64_t s_full[2];   // [tile]: S of the chunk is in TMEM
   uint64_t p_full[2];   // [tile]: the tile's 4 softmax warps wrote P
   uint64_t pv_done[2];  // [tile]: P.V of the chunk completed
@@ -347,7 +351,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       mbar_init(&bars->o_full[i], 1);
     }
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bars->kv_full[i], 1);
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->kv_empty[i], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -383,8 +388,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     }
     __syncwarp();
     uint32_t qi = 0, kv = 0, q_armed = 0;
-    // per K/V full barrier: bit i of kv_used = armed at least once, bit i of
-    // kv_par = parity of its most recently armed phase (registers, no arrays)
+    // per K/V stage (its K and V barriers are armed together): bit i of
+    // kv_used = armed at least once, bit i of kv_par = parity of its most
+    // recently armed phase (registers, no arrays)
     uint32_t kv_used = 0, kv_par = 0;
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
@@ -420,11 +426,13 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx_elect(&bars->kv_full[s], 2 * kChunkBytes);
         kv_par = (kv_used & (1u << s)) ? (kv_par ^ (1u << s)) : kv_par;
         kv_used |= 1u << s;
-        tma_load_4d_elect(k_smem + s * kChunkBytes, &p.tm_k, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
-        tma_load_4d_elect(v_smem + s * kChunkBytes, &p.tm_v, &bars->kv_full[s], 0, it.kvh, c * kChunk, it.b);
+        uint64_t* v_bar = kSplit ? &bars->v_full[s] : &bars->k_full[s];
+        mbar_arrive_expect_tx_elect(&bars->k_full[s], kSplit ? kChunkBytes : 2 * kChunkBytes);
+        tma_load_4d_elect(k_smem + s * kChunkBytes, &p.tm_k, &bars->k_full[s], 0, it.kvh, c * kChunk, it.b);
+        if (kSplit) mbar_arrive_expect_tx_elect(v_bar, kChunkBytes);
+        tma_load_4d_elect(v_smem + s * kChunkBytes, &p.tm_v, v_bar, 0, it.kvh, c * kChunk, it.b);
         ++kv;
       }
       ++qi;
@@ -436,8 +444,12 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       const uint32_t uses = (q_armed + 1 - b) / 2;
       if (uses > 0) bounded_wait(&bars->q_full[b], (uses - 1) & 1, abort_flag, false);
     }
-    for (int s = 0; s < kStages; ++s)
-      if (kv_used & (1u << s)) bounded_wait(&bars->kv_full[s], (kv_par >> s) & 1u, abort_flag, false);
+    for (int s = 0; s < kStages; ++s) {
+      if (kv_used & (1u << s)) {
+        bounded_wait(&bars->k_full[s], (kv_par >> s) & 1u, abort_flag, false);
+        if (kSplit) bounded_wait(&bars->v_full[s], (kv_par >> s) & 1u, abort_flag, false);
+      }
+    }
     __syncwarp();
   } else if (warp == WL::kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
@@ -483,9 +495,9 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
                           (j > 0 || k > 0) ? 1u : 0u, k < nk ? 1u : 0u);
           umma_commit_elect(&bars->pv_done[t]);
         };
-        auto wait_kv = [&](int j) {
+        auto wait_kv = [&](uint64_t* full, int j) {  // K or V of chunk j landed
           const uint32_t n = kv + j;
-          if (!__all_sync(kFullMask, bounded_wait<kWaitMma>(&bars->kv_full[n % kStages], (n / kStages) & 1, abort_flag)))
+          if (!__all_sync(kFullMask, bounded_wait<kWaitMma>(&full[n % kStages], (n / kStages) & 1, abort_flag)))
             return false;
           tc_fence_after();
           return true;
@@ -503,7 +515,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         // S of chunk 0 is issued after the previous item's last P.V, which
         // read P from the same columns; tcgen05.mma operations of one thread
         // execute in issue order, so no completion wait is needed in between.
-        if (!wait_kv(0)) { ok = false; break; }
+        if (!wait_kv(bars->k_full, 0)) { ok = false; break; }
         issue_s(0, cur, 0);
         if (two) issue_s(1, cur, 0);
         while (cur >= 0) {
@@ -511,9 +523,10 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           // per tile: P of chunk j ready -> O += P V(j), then S of chunk j+1
           // over the S/P columns (in issue order after the product reading P)
           if (!wait_p(0)) { ok = false; break; }
+          if (kSplit && !wait_kv(bars->v_full, j)) { ok = false; break; }
           issue_pv(0, cur, j);
           if (nxt >= 0) {
-            if (!wait_kv(j + 1)) { ok = false; break; }
+            if (!wait_kv(bars->k_full, j + 1)) { ok = false; break; }
             issue_s(0, nxt, j + 1);
           } else {
             // tile 0's O is final once its last P.V completes: its epilogue
@@ -878,6 +891,12 @@ __global__ void zero_rows(__nv_bfloat16* o, long long o_sb, long long o_sm, long
 // sum_s l_s 2^(m_s - m*) (any common m*) and O = sum_s w_s (O_s / l_s) /
 // sum_s w_s with w_s = l_s 2^(m_s - m*). Splits with l_s = 0 saw no visible
 // key and are skipped; a row with none left is written as zeros.
+// The kernel is a chain of L2 round trips, so the loads of kCombineBatch
+// splits are issued together: with at most that many splits every (m_s, l_s)
+// and partial row is in flight at once (one round trip), otherwise one round
+// trip for the maximum per batch and one for the sums. The sums run over s in
+// ascending order whatever the batching.
+constexpr int kCombineBatch = 8;
 __global__ void __launch_bounds__(256) combine_splits(const __nv_bfloat16* __restrict__ part,
                                                       const float2* __restrict__ ml,
                                                       __nv_bfloat16* o, long long o_sb, long long o_sm,
@@ -890,24 +909,56 @@ __global__ void __launch_bounds__(256) combine_splits(const __nv_bfloat16* __res
   const long long r = tid >> 3;
   const int q = static_cast<int>(tid & 7);
   if (r >= rows) return;
+  float2 v[kCombineBatch];
+  uint4 u[kCombineBatch];
+  auto load_ml = [&](int s0) {
+#pragma unroll
+    for (int i = 0; i < kCombineBatch; ++i)
+      v[i] = s0 + i < splits ? ml[(s0 + i) * rows + r] : make_float2(-INFINITY, 0.f);
+  };
+  auto load_part = [&](int s0) {
+#pragma unroll
+    for (int i = 0; i < kCombineBatch; ++i)
+      u[i] = s0 + i < splits
+                 ? *reinterpret_cast<const uint4*>(part + ((s0 + i) * rows + r) * 64 + q * 8)
+                 : make_uint4(0, 0, 0, 0);
+  };
   float mx = -INFINITY;
-  for (int s = 0; s < splits; ++s) {
-    const float2 v = ml[s * rows + r];
-    if (v.y > 0.f) mx = fmaxf(mx, v.x);
-  }
+  auto batch_max = [&]() {
+#pragma unroll
+    for (int i = 0; i < kCombineBatch; ++i)
+      if (v[i].y > 0.f) mx = fmaxf(mx, v[i].x);
+  };
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float wsum = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float2 v = ml[s * rows + r];
-    if (!(v.y > 0.f)) continue;
-    const float w = exp2f(v.x - mx) * v.y;
-    wsum += w;
-    const uint4 u = *reinterpret_cast<const uint4*>(part + (s * rows + r) * 64 + q * 8);
-    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+  auto accumulate = [&]() {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      acc[2 * e] += w * __uint_as_float(uw[e] << 16);
-      acc[2 * e + 1] += w * __uint_as_float(uw[e] & 0xffff0000u);
+    for (int i = 0; i < kCombineBatch; ++i) {
+      if (!(v[i].y > 0.f)) continue;
+      const float w = exp2f(v[i].x - mx) * v[i].y;
+      wsum += w;
+      const uint32_t uw[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += w * __uint_as_float(uw[e] << 16);
+        acc[2 * e + 1] += w * __uint_as_float(uw[e] & 0xffff0000u);
+      }
+    }
+  };
+  if (splits <= kCombineBatch) {
+    load_ml(0);
+    load_part(0);
+    batch_max();
+    accumulate();
+  } else {
+    for (int s0 = 0; s0 < splits; s0 += kCombineBatch) {
+      load_ml(s0);
+      batch_max();
+    }
+    for (int s0 = 0; s0 < splits; s0 += kCombineBatch) {
+      load_ml(s0);
+      load_part(s0);
+      accumulate();
     }
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
