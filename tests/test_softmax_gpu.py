@@ -73,6 +73,28 @@ def test_c2_sweep_bf16(rows, cols):
     assert ((sums - 1).abs() < 2e-2 + cols * 4e-3 * 2 ** -8).all()
 
 
+# More wide rows than the GPU holds blocks for at once (several waves of one
+# block per row): sampled rows against the oracle, every row's sum, and rows
+# of whole 16-byte vectors exactly as a short call of the same rows computes
+# them (a ragged row's segmentation depends on its address, so a short call of
+# such rows may take another path).
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,cols", [(1024, 32768), (4097, 8192), (3000, 1032), (2000, 4096),
+                                       (700, 20008), (700, 20001)])
+def test_many_wide_rows_match_short_calls(rows, cols, dtype):
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = (torch.randn(rows, cols, device="cuda", generator=g) * 4).to(dtype)
+    out = softmax(x, 4)
+    idx = torch.cat([torch.arange(0, 8), torch.arange(rows - 8, rows),
+                     torch.randint(0, rows, (48,), generator=torch.Generator().manual_seed(2))])
+    check(out[idx.cuda()], x[idx.cuda()], dtype)
+    sums = out.float().sum(-1)
+    assert ((sums - 1).abs() < 2e-2 + cols * 4e-3 * 2 ** -8).all()
+    if cols % 8 == 0:
+        for r0 in (0, rows // 2, rows - 16):
+            assert torch.equal(out[r0:r0 + 16], softmax(x[r0:r0 + 16], 4)), r0
+
+
 def test_c2_narrow_many_rows_bf16():
     rows, cols = wl.C2_NARROW
     x = wl.softmax_c2(rows, cols, seed=3)
