@@ -82,10 +82,11 @@ def _rank_main(rank: int, world: int, port: int, B: int, result_path: str):
 
 
 @pytest.mark.parametrize("B", [256, 253])
-def test_sharded_batch_matches_one_gpu(B, tmp_path):
+def test_sharded_batch_matches_one_gpu(B, tmp_path, monkeypatch):
     world = min(torch.cuda.device_count(), 8)
     path = str(tmp_path / "res.txt")
-    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    # the spawned ranks inherit it: plain peer transfers, no NVLink multicast
+    monkeypatch.setenv("NCCL_NVLS_ENABLE", "0")
     mp.start_processes(_rank_main, args=(world, _free_port(), B, path), nprocs=world,
                        start_method="spawn", join=True)
     same_attn, same_softmax, within, err = open(path).read().split()
