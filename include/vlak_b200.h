@@ -11,7 +11,8 @@
  *
  * Inputs are borrowed for the duration of the launch; outputs are written in
  * place and owned by the caller. None of the entry points allocates device
- * memory.
+ * memory (the first attention launch allocates one 4-byte pinned host word,
+ * see vlak_device_error_poll).
  */
 #ifndef VLAK_B200_H_
 #define VLAK_B200_H_
@@ -50,12 +51,26 @@ VLAK_API const char* vlak_status_string(int status);
 VLAK_API const char* vlak_last_error_message(void);
 
 /*
- * Device error word. Kernels whose waits are bounded record a failed wait
- * here instead of hanging; the word is per device and sticky until read.
- * vlak_device_error_read() copies it to *code (0 = none) and clears it. It is
- * a synchronous call on the current device (use it between steps, not inside
- * a captured graph).
+ * Device error reporting. Kernels whose waits are bounded (the attention
+ * kernels) record a failed wait instead of hanging: VLAK_ERR_DEVICE_TIMEOUT,
+ * sticky until read, and that launch's output is incomplete.
+ *  - The status goes to a pinned, device-mapped host word of the process
+ *    (4 bytes, allocated once by the first attention launch that is not being
+ *    stream-captured; shared by all devices).
+ *  - A launch made before that word exists (the first call of the process
+ *    inside a stream capture) records into a per-device word instead.
+ * vlak_device_error_poll() reads the host word without synchronizing
+ * anything: it sees the failures of kernels that have finished, copies the
+ * status to *code (0 = none) and clears it. The torch ops call it on entry
+ * and raise RuntimeError when it is set. Replaces nothing in the reference,
+ * which checks only cudaGetLastError after each launch
+ * (kernels/attention/fused_attention.cu:594-596).
  */
+VLAK_API int vlak_device_error_poll(int* code);
+
+/* Synchronous form: reads and clears the per-device word of the current
+ * device (a blocking copy, so call it between steps, not inside a stream
+ * capture) and the host word; *code is the status found (0 = none). */
 VLAK_API int vlak_device_error_read(int* code);
 
 /* ------------------------------------------------------------------------
@@ -199,7 +214,10 @@ VLAK_API int vlak_attn_gqa_masked_fwd_ws(const vlak_attn_gqa_args* args, const v
  *  - Every call on a device shares the buffer: calls whose GPU work overlaps
  *    (different streams) race on it and corrupt each other's results; keep
  *    them ordered on one stream. No part of it has to start at zero: a call
- *    writes every entry its merge reads. */
+ *    writes every entry its merge reads.
+ *  - It does not set up the host error word either: a failed wait is
+ *    reported there only if an earlier call of another entry point created
+ *    it, else in the per-device word (vlak_device_error_read). */
 VLAK_API int vlak_attn_gqa_fwd_noalloc(const vlak_attn_gqa_args* args, void* stream);
 
 /* Non-GQA attention on the CUDA cores with fp32 math: the v1 path of
@@ -218,9 +236,9 @@ VLAK_API int vlak_attn_fwd(const void* q, const void* k, const void* v, void* o,
 /* Self-test of the bounded device waits. No counterpart in the reference:
  * a test hook for the failure path that replaces a hang. Launches, on
  * `stream`, one kernel that waits on a barrier nothing completes; after the
- * 1 s wait limit it records VLAK_ERR_DEVICE_TIMEOUT in the device error word
- * (read it with vlak_device_error_read) and returns, leaving the context
- * usable. */
+ * 1 s wait limit it records VLAK_ERR_DEVICE_TIMEOUT as a failed attention
+ * wait would (read it with vlak_device_error_poll or vlak_device_error_read)
+ * and returns, leaving the context usable. */
 VLAK_API int vlak_selftest_wait_timeout(void* stream);
 
 #ifdef __cplusplus

@@ -48,6 +48,7 @@ def lib():
     L.vlak_attn_gqa_check.argtypes = [ctypes.POINTER(GqaArgs), ctypes.POINTER(ctypes.c_int64),
                                       ctypes.POINTER(ctypes.c_float)]
     L.vlak_device_error_read.argtypes = [ctypes.POINTER(ctypes.c_int)]
+    L.vlak_device_error_poll.argtypes = [ctypes.POINTER(ctypes.c_int)]
     L.vlak_attn_gqa_workspace_size.argtypes = [ctypes.POINTER(GqaArgs), ctypes.POINTER(ctypes.c_int64)]
     L.vlak_attn_gqa_fwd_ws.argtypes = [ctypes.POINTER(GqaArgs), ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_void_p]
@@ -65,10 +66,13 @@ def lib():
     return L
 
 
-def declared_symbols() -> list[str]:
-    """Every function the public header declares."""
-    text = open(HEADER).read()
-    return sorted(set(re.findall(r"VLAK_API\s+[\w\s\*]+?\b(vlak_\w+)\s*\(", text)))
+CMP_HEADER = os.path.join(os.path.dirname(HEADER), "vlak_comparators.h")
+
+
+def declared_symbols(header: str = HEADER, macro: str = "VLAK_API") -> list[str]:
+    """Every function a public header declares."""
+    text = open(header).read()
+    return sorted(set(re.findall(macro + r"\s+[\w\s\*]+?\b(vlak_\w+)\s*\(", text)))
 
 
 def gqa_args(q, k, v, o, prefix_len=-1, dead_start=0, dead_end=0, scale=-1.0,

@@ -68,13 +68,23 @@
 
 namespace vlak {
 
-// Device error word of this library (see vlak_device_error_read).
+// Device error word of this library (see vlak_device_error_read). Used when
+// a launch has no host-mapped error word (see host_error_word).
 __device__ int g_device_error = 0;
 
 namespace {
 
-__device__ __forceinline__ void record_device_error(int code) {
-  atomicCAS(&g_device_error, 0, code);
+// Records a failed wait where the host can see it: in the process's
+// host-mapped error word when the launch has one (read without any device
+// synchronization by vlak_device_error_poll, which the torch ops call on
+// entry), else in the device error word.
+__device__ __forceinline__ void publish_device_error(int* host_err, int code) {
+  if (host_err != nullptr) {
+    *reinterpret_cast<volatile int*>(host_err) = code;
+    __threadfence_system();
+  } else {
+    atomicCAS(&g_device_error, 0, code);
+  }
 }
 
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s per wait
@@ -105,7 +115,7 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity,
       uint64_t t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       if (t - t0 > kWaitLimitNs) {
-        record_device_error(VLAK_ERR_DEVICE_TIMEOUT);
+        // reported by the CTA's thread 0 once every role has drained
         *abort_flag = 1;
         return false;
       }
@@ -204,6 +214,7 @@ struct __align__(64) Params {
   int num_items;
   int P, ds, de;
   float scale_log2;  // softmax scale * log2(e)
+  int* host_err;     // host-mapped error word of the process, or nullptr
   // mask mode 1: per-sample lengths (B,), int32 or int64, in device memory
   const void* lengths;
   int lengths_i64;
@@ -866,6 +877,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) publish_device_error(p.host_err, VLAK_ERR_DEVICE_TIMEOUT);
   if (warp == WL::kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -1017,14 +1029,15 @@ static int validate(const vlak_attn_gqa_args* a, int64_t* P_out, float* scale_ou
   if (P > a->N) return set_error(VLAK_ERR_INVALID_ARGUMENT, "prefix_len exceeds kv length");
   if (!(0 <= a->dead_start && a->dead_start <= a->dead_end && a->dead_end <= P))
     return set_error(VLAK_ERR_INVALID_ARGUMENT, "dead band must satisfy 0 <= ds <= de <= prefix_len");
+  // The reference requires this for its cp.async tiles; the same condition
+  // is what TMA tensor maps need here (16-byte base and byte strides).
   const void* ptrs[4] = {a->q, a->k, a->v, a->o};
   const int64_t* strides[4] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride};
+  constexpr const char* kAlignMsg = "strides/base must keep 16B alignment (TMA tensor maps)";
   for (int i = 0; i < 4; ++i) {
-    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0)
-      return set_error(VLAK_ERR_ALIGNMENT, "strides/base must keep 16B alignment for cp.async");
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0) return set_error(VLAK_ERR_ALIGNMENT, kAlignMsg);
     for (int d = 0; d < 3; ++d)
-      if (strides[i][d] % 8 != 0)
-        return set_error(VLAK_ERR_ALIGNMENT, "strides/base must keep 16B alignment for cp.async");
+      if (strides[i][d] % 8 != 0) return set_error(VLAK_ERR_ALIGNMENT, kAlignMsg);
   }
   if (P_out) *P_out = P;
   if (scale_out) *scale_out = a->scale > 0 ? static_cast<float>(a->scale) : 0.125f;
@@ -1041,6 +1054,7 @@ struct MaskSpec {
   int64_t mask_sb = 0, mask_sm = 0;
   void* workspace = nullptr;  // key-split partials (nullptr: never split)
   int64_t workspace_bytes = 0;
+  bool no_alloc = false;      // never set up the host error word here
 };
 
 // Query tiling of an item: MT query positions per M-tile, 1 or 2 M-tiles per
@@ -1197,6 +1211,7 @@ static int launch_gqa(const vlak_attn_gqa_args* a_in, void* stream, const MaskSp
   prm.ds = static_cast<int>(a->dead_start);
   prm.de = static_cast<int>(a->dead_end);
   prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.host_err = host_error_word(cs, !ms.no_alloc);
   prm.o = o;
   prm.o_sb = a->o_stride[0];
   prm.o_sm = a->o_stride[1];
@@ -1296,7 +1311,7 @@ namespace {
 // that nothing arrives on. The wait runs out after its limit, records
 // VLAK_ERR_DEVICE_TIMEOUT in the device error word and the kernel returns
 // normally, so the context stays usable.
-__global__ void wait_timeout_selftest() {
+__global__ void wait_timeout_selftest(int* host_err) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
@@ -1305,14 +1320,16 @@ __global__ void wait_timeout_selftest() {
     fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) bounded_wait(&bar, 0, &abort_flag);
+  if (threadIdx.x == 0 && !bounded_wait(&bar, 0, &abort_flag))
+    publish_device_error(host_err, VLAK_ERR_DEVICE_TIMEOUT);
 }
 
 }  // namespace
 
 int selftest_wait_timeout(void* stream) {
   clear_error();
-  wait_timeout_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  wait_timeout_selftest<<<1, 32, 0, cs>>>(host_error_word(cs));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("wait_timeout_selftest launch failed", e);
   return VLAK_OK;
@@ -1446,6 +1463,7 @@ extern "C" int vlak_attn_gqa_fwd_noalloc(const vlak_attn_gqa_args* args, void* s
                       "with a workspace instead",
                       static_cast<long long>(need), static_cast<long long>(kNoAllocScratchBytes));
   MaskSpec ms;
+  ms.no_alloc = true;
   if (need > 0) {
     st = noalloc_scratch(&ms.workspace);
     if (st != VLAK_OK) return st;
@@ -1455,12 +1473,16 @@ extern "C" int vlak_attn_gqa_fwd_noalloc(const vlak_attn_gqa_args* args, void* s
 }
 
 extern "C" int vlak_device_error_read(int* code) {
+  vlak::clear_error();
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, vlak::g_device_error, sizeof(int));
   if (e != cudaSuccess) return vlak::set_cuda_error("vlak_device_error_read", e);
   const int zero = 0;
   e = cudaMemcpyToSymbol(vlak::g_device_error, &zero, sizeof(int));
   if (e != cudaSuccess) return vlak::set_cuda_error("vlak_device_error_read", e);
-  if (code) *code = v;
+  // the host-mapped word of the process (cleared as well)
+  int h = 0;
+  vlak_device_error_poll(&h);
+  if (code) *code = v != 0 ? v : h;
   return VLAK_OK;
 }

@@ -6,6 +6,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -80,7 +81,55 @@ int current_device_info(DeviceInfo* out) {
   return status;
 }
 
+namespace {
+std::mutex g_host_word_mu;
+std::atomic<int*> g_host_word{nullptr};
+}  // namespace
+
+int* host_error_word(cudaStream_t stream, bool may_allocate) {
+  int* w = g_host_word.load(std::memory_order_acquire);
+  if (w != nullptr || !may_allocate) return w;
+  // cudaHostAlloc is not allowed while the stream is being captured (it
+  // would invalidate the capture): such a launch reports through the device
+  // word instead
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_host_word_mu);
+  w = g_host_word.load(std::memory_order_acquire);
+  if (w != nullptr) return w;
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  // unified addressing: the device sees the word at its host address
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, p, 0) != cudaSuccess || d != p) {
+    cudaGetLastError();
+    cudaFreeHost(p);
+    return nullptr;
+  }
+  *static_cast<volatile int*>(p) = 0;
+  g_host_word.store(static_cast<int*>(p), std::memory_order_release);
+  return static_cast<int*>(p);
+}
+
 }  // namespace vlak
+
+extern "C" int vlak_device_error_poll(int* code) {
+  int v = 0;
+  int* w = vlak::g_host_word.load(std::memory_order_acquire);
+  if (w != nullptr) {
+    volatile int* vw = w;
+    v = *vw;
+    if (v != 0) *vw = 0;
+  }
+  if (code) *code = v;
+  return VLAK_OK;
+}
 
 extern "C" int vlak_abi_version(void) { return VLAK_ABI_VERSION; }
 

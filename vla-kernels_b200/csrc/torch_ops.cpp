@@ -6,10 +6,12 @@
 // Schemas: kernels/softmax/softmax_kernels.cu:303-305,
 //          kernels/attention/fused_attention.cu:671-676,
 //          kernels/attention/fused_attention_v4.cu:333-336;
-// plus one additive schema with no counterpart in the reference,
-// fused_attention_gqa_varlen (per-sample lengths).
+// plus two additive schemas with no counterpart in the reference:
+// fused_attention_gqa_varlen (per-sample lengths) and device_error (the
+// synchronous check of the bounded-wait error words).
 
 #include <ATen/ATen.h>
+#include <c10/cuda/CUDAFunctions.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
@@ -26,6 +28,27 @@ void check_status(int status, const char* op) {
               vlak_status_string(status), ")");
 }
 
+// Every op first reads the host-mapped error word (no device
+// synchronization): a bounded wait that ran out in an attention kernel which
+// has finished since is raised here, on the caller's next op, instead of
+// going unnoticed. The word is cleared by the read, so the following call
+// runs normally.
+void raise_pending_device_error(const char* op) {
+  int code = VLAK_OK;
+  vlak_device_error_poll(&code);
+  TORCH_CHECK(code == VLAK_OK, op, ": an earlier vlak kernel gave up a bounded device wait (",
+              vlak_status_string(code), "); the output of that call is incomplete");
+}
+
+// vlak::device_error(): the synchronous check. Waits for the device, then
+// reads and clears the error words; returns the status found (0 = none).
+int64_t device_error() {
+  int code = VLAK_OK;
+  c10::cuda::device_synchronize();
+  check_status(vlak_device_error_read(&code), "vlak::device_error");
+  return code;
+}
+
 int dtype_code(at::ScalarType t) {
   switch (t) {
     case at::kFloat: return VLAK_F32;
@@ -38,6 +61,7 @@ int dtype_code(at::ScalarType t) {
 
 // kernels/softmax/softmax_kernels.cu:255-297
 at::Tensor softmax_lastdim(const at::Tensor& x_in, int64_t version) {
+  raise_pending_device_error("vlak::softmax");
   TORCH_CHECK(x_in.is_cuda(), "input must be CUDA");
   TORCH_CHECK(x_in.dim() == 2, "expected a 2D [rows, cols] tensor");
   const int dt = dtype_code(x_in.scalar_type());
@@ -103,6 +127,7 @@ int64_t ws_bytes(const at::Tensor& ws) { return ws.defined() ? ws.numel() : 0; }
 
 at::Tensor run_gqa(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
                    int64_t prefix_len, int64_t dead_start, int64_t dead_end, bool v4) {
+  raise_pending_device_error(v4 ? "vlak::fused_attention_gqa_v4" : "vlak::fused_attention_gqa");
   const char* op = v4 ? "v4" : "v3";
   vlak_attn_gqa_args a = gqa_args(q, k, v, scale, prefix_len, dead_start, dead_end, op);
   c10::cuda::CUDAGuard guard(q.device());
@@ -142,6 +167,7 @@ at::Tensor fused_attention_gqa_v4(const at::Tensor& q, const at::Tensor& k, cons
 at::Tensor fused_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
                            double scale, const std::optional<at::Tensor>& attn_mask,
                            int64_t prefix_len) {
+  raise_pending_device_error("vlak::fused_attention");
   TORCH_CHECK(q_in.is_cuda() && q_in.dim() == 4, "expected 4D CUDA (B,H,M,D)");
   TORCH_CHECK(q_in.size(3) == 64, "this kernel is specialized to head_dim 64");
   TORCH_CHECK(k_in.dim() == 4 && v_in.dim() == 4 && k_in.size(3) == 64 && v_in.size(3) == 64,
@@ -209,6 +235,7 @@ at::Tensor fused_attention(const at::Tensor& q_in, const at::Tensor& k_in, const
 at::Tensor fused_attention_gqa_varlen(const at::Tensor& q, const at::Tensor& k,
                                       const at::Tensor& v, const at::Tensor& lengths_in,
                                       double scale) {
+  raise_pending_device_error("vlak::fused_attention_gqa_varlen");
   vlak_attn_gqa_args a = gqa_args(q, k, v, scale, -1, 0, 0, "fused_attention_gqa_varlen");
   TORCH_CHECK(lengths_in.is_cuda() && lengths_in.device() == q.device(),
               "lengths must be on the device of q");
@@ -241,12 +268,17 @@ TORCH_LIBRARY_FRAGMENT(vlak, m) {
       "fused_attention_gqa_varlen(Tensor q, Tensor k, Tensor v, Tensor lengths, "
       "float scale=-1.) -> Tensor");
   m.def("softmax(Tensor x, int version=4) -> Tensor");
+  m.def("device_error() -> int");
   m.def(
       "fused_attention_gqa(Tensor q, Tensor k, Tensor v, float scale=-1., "
       "int prefix_len=-1, int dead_start=0, int dead_end=0) -> Tensor");
   m.def(
       "fused_attention_gqa_v4(Tensor q, Tensor k, Tensor v, float scale=-1., "
       "int prefix_len=-1, int dead_start=0, int dead_end=0) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(vlak, CompositeExplicitAutograd, m) {
+  m.impl("device_error", &device_error);
 }
 
 TORCH_LIBRARY_IMPL(vlak, CUDA, m) {

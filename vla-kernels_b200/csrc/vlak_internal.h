@@ -32,4 +32,12 @@ struct DeviceInfo {
 };
 int current_device_info(DeviceInfo* out);
 
+// The process's host-mapped error word (pinned, device-mapped, portable to
+// every device), allocated on first use; nullptr when it is not set up yet
+// and `stream` is capturing (no allocation happens during a capture) or when
+// the allocation failed. Kernels write a failed bounded wait's status there;
+// vlak_device_error_poll reads it without synchronizing the device. With
+// may_allocate false it only returns a word set up earlier (or nullptr).
+int* host_error_word(cudaStream_t stream, bool may_allocate = true);
+
 }  // namespace vlak

@@ -104,14 +104,18 @@ def fused_attention_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                         prefix_len: int | None = None,
                         dead_start: int = 0,
                         dead_end: int = 0) -> torch.Tensor:
-    """GQA-native SDPA over the model's projection layouts.
+    """Attention where H query heads share H_kv key/value heads.
 
-    q is (B, M, H, 64); k/v are (B, N, H_kv, 64) with H a multiple of H_kv,
-    consumed at their natural strides (no transpose/contiguous/expand). The
-    mask is arithmetic: visible(r, c) = c < prefix_len ? (c < dead_start or
-    c >= dead_end) : c <= (N - M) + r. Returns (B, M, H, 64) contiguous, so
-    .reshape(B, M, H*64) is a view. bf16 only. Rows with no visible key are
-    exact zeros.
+    Inputs stay in the layout the projections produce: queries (B, M, H, 64)
+    and keys / values (B, N, H_kv, 64), bf16, read in place at whatever
+    strides they have (head_dim must be the unit-stride dim). Query head h
+    uses kv head h // (H // H_kv). No mask tensor: key c is visible to query
+    row r when c < prefix_len and c lies outside [dead_start, dead_end), or
+    when c >= prefix_len and c <= (N - M) + r (a causal staircase over the
+    trailing keys). prefix_len defaults to N and scale to 1/8.
+
+    The result is a new contiguous (B, M, H, 64) tensor, so flattening the
+    heads is a free view. A row that sees no key at all comes back as zeros.
     """
     _ensure_registered()
     return torch.ops.vlak.fused_attention_gqa(
@@ -129,3 +133,25 @@ def fused_attention_gqa_v4(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return torch.ops.vlak.fused_attention_gqa_v4(
         q, k, v, -1.0 if scale is None else scale,
         -1 if prefix_len is None else prefix_len, dead_start, dead_end)
+
+
+def device_error() -> int:
+    """Synchronous check of the bounded device waits: waits for the device,
+    then reads and clears the error words. Returns the status code of a wait
+    that ran out since the last check (5, VLAK_ERR_DEVICE_TIMEOUT), else 0.
+
+    Each op also reads the host-mapped error word on entry, without any
+    synchronization, and raises RuntimeError when a kernel that has finished
+    since the previous op gave up a wait; this call is for callers that want
+    to know at a point of their choosing (e.g. after replaying a CUDA graph,
+    whose replays run no host code)."""
+    _native.load_ops()
+    return int(torch.ops.vlak.device_error())
+
+
+def check_device_error() -> None:
+    """device_error(), raising RuntimeError when a wait ran out."""
+    code = device_error()
+    if code != 0:
+        raise RuntimeError(f"vlak: a kernel gave up a bounded device wait (status {code}); "
+                           "the output of that call is incomplete")
