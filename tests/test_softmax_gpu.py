@@ -180,3 +180,41 @@ def test_patch_kernels_style_call():
     x = torch.randn(2, 15, 50, 291, device="cuda")
     out = softmax(x.reshape(-1, 291), "auto").reshape(x.shape)
     torch.testing.assert_close(out, torch.softmax(x, -1), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("version", list(VERSIONS))
+@pytest.mark.parametrize("shape", [(64, 291), (8, 1024), (8, 4096), (4, 16384), (2, 32768)])
+def test_bf16_keeps_tail_probabilities(version, shape):
+    """A wide logit spread puts most probabilities far below 2^-24. Each must
+    come out within a relative tolerance of the fp64 oracle, as torch.softmax
+    keeps them, not flushed to zero. Bound: the exp and the normalised value
+    are each rounded to bf16 once (2 x 2^-9), plus fp32 arithmetic: 1e-2."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = (torch.rand(*shape, device="cuda", generator=g) * -60.0).to(torch.bfloat16)
+    out = softmax(x, version=version).double().cpu().numpy()
+    ref = softmax_rows(x.float().cpu().numpy())
+    keep = ref >= 1e-36  # bf16 normal range, away from its subnormals
+    assert keep.mean() > 0.5
+    rel = np.abs(out[keep] - ref[keep]) / ref[keep]
+    assert rel.max() <= 1e-2, f"max rel err {rel.max()} on probabilities down to {ref[keep].min()}"
+    assert (out[keep] > 0).all(), "a probability torch keeps was flushed to zero"
+
+
+@pytest.mark.parametrize("which", ["cudnn", "cub"])
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", [(1, 16), (33, 241), (256, 1000), (4, 4096), (2, 32768)])
+def test_library_comparators_match_oracle(which, dtype, shape):
+    """softmax_cudnn / softmax_cub (benchmark bars) compute the same softmax:
+    fp32 within torch's fp32 tolerance (rtol 1e-5, atol 1e-6), fp16 / bf16
+    within atol 1e-2, rtol 1.6e-2 of the fp64 oracle."""
+    from kernels.softmax import softmax_cub, softmax_cudnn
+
+    fn = softmax_cudnn if which == "cudnn" else softmax_cub
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = (torch.randn(*shape, device="cuda", generator=g) * 3).to(dtype)
+    out = fn(x).double().cpu()
+    ref = torch.from_numpy(softmax_rows(x.float().cpu().numpy()))
+    if dtype == torch.float32:
+        torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-6)
+    else:
+        torch.testing.assert_close(out, ref, atol=1e-2, rtol=1.6e-2)

@@ -31,6 +31,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "vlak_device.cuh"
 #include "vlak_internal.h"
 
@@ -222,8 +224,12 @@ template <> struct Pair2<__nv_bfloat16> {
   }
 };
 
-// exp values of a row in (0, 1] held as f16 pairs (11 significant bits; below
-// 2^-14 an absolute error under 2^-25), between the sum and the output pass
+// exp values of a row in (0, 1], held as pairs of the row's own 2-byte type
+// between the sum and the output pass. fp16 rows keep f16 pairs (11
+// significant bits; below 2^-14 an absolute error under 2^-25, which is also
+// where fp16 outputs lose their own precision). bf16 rows keep bf16 pairs:
+// 8 significant bits but bf16's 8-bit exponent, so tail probabilities far
+// below 2^-24 survive, as they do in torch.softmax.
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -233,16 +239,36 @@ __device__ __forceinline__ void unpack_f16x2(uint32_t u, float& lo, float& hi) {
   asm("{\n\t.reg .f16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.f32.f16 %0, l;\n\tcvt.f32.f16 %1, h;\n\t}"
       : "=f"(lo), "=f"(hi) : "r"(u));
 }
+template <typename T>
+__device__ __forceinline__ uint32_t pack_exp2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  } else {
+    return pack_f16x2(lo, hi);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void unpack_exp2(uint32_t u, float& lo, float& hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    lo = __uint_as_float(u << 16);  // bf16 -> f32 is a 16-bit shift
+    hi = __uint_as_float(u & 0xffff0000u);
+  } else {
+    unpack_f16x2(u, lo, hi);
+  }
+}
 
 // Register-resident row for 2-byte element types: the row stays in registers
 // as the raw 16-byte vectors (4 registers per 8 elements, half the footprint
 // of fp32 copies), so a 32768-column row fits 512 threads x 8 vectors at
 // under 64 registers and two rows share an SM. The max runs on packed pairs;
 // the sum pass evaluates each exp once and keeps it in the same registers as
-// an f16 pair, so the output pass only scales by 1 / sum: one MUFU operation
-// per element, which is what bounds wide rows at full HBM rate. The outputs
-// are the f16-rounded exps times the fp32 reciprocal, rounded to the output
-// type (within 2^-11 + one output ulp relative).
+// a pair of the row's type (pack_exp2), so the output pass only scales by
+// 1 / sum: one MUFU operation per element, which is what bounds wide rows at
+// full HBM rate. The outputs are the rounded exps times the fp32 reciprocal,
+// rounded to the output type (fp16: within 2^-11 + one output ulp relative;
+// bf16: within 2^-9 + one output ulp).
 template <typename T, int RV, int NT, class Group>
 __device__ __forceinline__ void row_softmax_reg_packed(const T* __restrict__ xr,
                                                        T* __restrict__ yr, int n, int t,
@@ -307,7 +333,7 @@ __device__ __forceinline__ void row_softmax_reg_packed(const T* __restrict__ xr,
           e1 = exp_shift<T>(f[2 * k + 1], m);
           s += e0 + e1;
         }
-        w[k] = pack_f16x2(e0, e1);
+        w[k] = pack_exp2<T>(e0, e1);
       }
       raw[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -333,7 +359,7 @@ __device__ __forceinline__ void row_softmax_reg_packed(const T* __restrict__ xr,
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         float a, b;
-        unpack_f16x2(w[k], a, b);
+        unpack_exp2<T>(w[k], a, b);
         if constexpr (kPairs) {
           f2_unpack(f2_mul(f2_pack(a, b), inv2), f[2 * k], f[2 * k + 1]);
         } else {
