@@ -66,17 +66,23 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str):
-    """Per-launch DRAM bytes of the attention kernel from the committed ncu
-    summary (profiles/<name>), line `traffic_bytes_per_launch: <int>`."""
-    path = os.path.join(REPO, "profiles", name)
-    try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return int(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+# The committed ncu capture of the attention kernel: the raw-page metrics of
+# two launches on the C3/C5 shapes at this batch (larger than L2), read by
+# roofline.py. DRAM traffic grows with the number of batch elements, so it is
+# scaled to a launch's batch.
+NCU_ATTN_CSV = os.path.join(REPO, "profiles", "gqa_attention_sm100_c5_b512.csv")
+NCU_ATTN_BATCH = 512
+
+
+def attention_traffic(batch: int):
+    """DRAM bytes (read + write) per launch of the attention kernel at
+    `batch`, from the committed ncu capture, or None."""
+    import roofline
+
+    if not os.path.exists(NCU_ATTN_CSV):
+        return None
+    t = roofline.kernel_traffic(NCU_ATTN_CSV, "gqa_attention_sm100")
+    return None if t is None else int(round(t * batch / NCU_ATTN_BATCH))
 
 
 class ClockSampler:
@@ -239,13 +245,14 @@ def bench_ours(args, rank, world, local):
     flops_per_launch = wl.attn_flops(shape)
     achieved_gbs = bytes_per_launch / launch_s / 1e9
     achieved_tflops = flops_per_launch / launch_s / 1e12
-    traffic = profile_traffic("gqa_attention_sm100_c5.txt")
-    if traffic is not None and world > 1:
-        traffic = int(traffic * B / GLOBAL_B)
+    traffic = attention_traffic(B)
     roofline = {
         "bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peaks["hbm_gbs"],
         "unit": "GB/s", "frac": round(achieved_gbs / peaks["hbm_gbs"], 4),
-        "traffic": traffic, "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
+        "traffic": traffic,
+        "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, median of the launches "
+                          f"in {os.path.relpath(NCU_ATTN_CSV, REPO)} (B={NCU_ATTN_BATCH}) scaled to "
+                          f"B={B}", "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
         if peak_src == "measured" else "fallback 6.65 TB/s",
         "kernel": "gqa_attention_sm100", "us_per_launch": round(launch_s * 1e6, 3),
         "algorithmic_bytes_per_launch": bytes_per_launch,
@@ -283,6 +290,8 @@ def bench_ours(args, rank, world, local):
         line["softmax"] = bench_softmax()
     if rank == 0 and world == 1 and not args.no_sites:
         line["sites"] = bench_sites()
+    if rank == 0 and world == 1 and not args.no_comparators:
+        line["comparators"] = bench_comparators()
     return line
 
 
@@ -460,18 +469,16 @@ def bench_sites():
     return res
 
 
-def time_softmax_flushed(x, iters: int = 10) -> float:
-    """Median seconds of softmax(x, "auto") with L2 flushed before every call:
-    a 256 MB write (larger than the 126 MB L2), then a 256 MB read of another
-    buffer, so the timed kernel starts with a cold L2 that holds no dirty lines
-    (their write-back would otherwise be charged to it)."""
-    from kernels.softmax import softmax
-
+def time_flushed(fn, iters: int = 10) -> float:
+    """Median seconds of fn() with L2 flushed before every call: a 256 MB
+    write (larger than the 126 MB L2), then a 256 MB read of another buffer,
+    so the timed kernel starts with a cold L2 that holds no dirty lines (their
+    write-back would otherwise be charged to it)."""
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
     clean = torch.ones(64 * 2**20, dtype=torch.float32, device="cuda")
     sink = torch.empty((), dtype=torch.float32, device="cuda")
     for _ in range(3):
-        softmax(x, "auto")
+        fn()
     times = []
     for _ in range(iters):
         flush.zero_()
@@ -479,12 +486,19 @@ def time_softmax_flushed(x, iters: int = 10) -> float:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        softmax(x, "auto")
+        fn()
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) / 1e3)
     del flush, clean
     return statistics.median(times)
+
+
+def time_softmax_flushed(x, iters: int = 10) -> float:
+    """time_flushed of softmax(x, "auto")."""
+    from kernels.softmax import softmax
+
+    return time_flushed(lambda: softmax(x, "auto"), iters)
 
 
 def bench_softmax():
@@ -516,6 +530,199 @@ def bench_softmax():
             one(f"C2_{rows}x{cols}", wl.softmax_c2(rows, cols))
     one(f"C2_narrow_{wl.C2_NARROW[0]}x{wl.C2_NARROW[1]}", wl.softmax_c2(*wl.C2_NARROW))
     return res
+
+
+REF_KERNELS = os.path.join(REPO, "baseline", "_ref", "kernels_sm100a")
+SOFTMAX_CMP_CASES = [("C1_fp32_4096x1024", None), ("C2_1024x4096", (1024, 4096)),
+                     ("C2_8192x4096", (8192, 4096)), ("C2_1024x16384", (1024, 16384)),
+                     ("C2_8192x16384", (8192, 16384)), ("C2_1024x32768", (1024, 32768)),
+                     ("C2_8192x32768", (8192, 32768)),
+                     (f"C2_narrow_{wl.C2_NARROW[0]}x{wl.C2_NARROW[1]}", wl.C2_NARROW)]
+
+
+def _softmax_case(shape):
+    return wl.softmax_c1() if shape is None else wl.softmax_c2(*shape)
+
+
+def sdpa_gqa_call(q, k, v, mask):
+    """torch SDPA on the op's (B, M, H, 64) / (B, N, Hkv, 64) tensors: views
+    to (B, H, M, 64), torch's own GQA (enable_gqa) and the analytic mask as a
+    (1, 1, M, N) bool tensor."""
+    import torch.nn.functional as F
+
+    return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                          attn_mask=mask, scale=0.125, enable_gqa=True)
+
+
+def expert_mask(s, device="cuda"):
+    r = torch.arange(s.M, device=device)[:, None]
+    c = torch.arange(s.N, device=device)[None, :]
+    vis = torch.where(c < s.P, (c < s.ds) | (c >= s.de), c <= (s.N - s.M) + r)
+    return vis[None, None]
+
+
+def bench_comparators() -> dict:
+    """Bars measured on the same GPU in the same run, reported beside the
+    headline and not the target: torch.softmax, cuDNN and CUB softmax over
+    C1 / the wide and narrow C2 cases (L2 flushed, as the softmax lines);
+    torch SDPA (its own GQA, bool mask) at C3 B=64 and C5 B=2048; the
+    L2-warm roof of C3 B=64 (one input set replayed, our kernel); and the
+    reference's own kernels rebuilt for sm_100a, timed in a separate process
+    (their op schemas collide with ours in one process)."""
+    from kernels.attention import fused_attention_gqa_v4
+    from kernels.softmax import softmax_cub, softmax_cudnn
+
+    peaks, _ = load_peaks()
+    res = {"note": "same-GPU bars, reported only"}
+    sm = {}
+    for name, shape in SOFTMAX_CMP_CASES:
+        x = _softmax_case(shape)
+        nbytes = wl.softmax_bytes(x.shape[0], x.shape[1], x.element_size())
+        row = {}
+        for label, fn in (("torch_softmax", lambda: torch.softmax(x, dim=-1)),
+                          ("cudnn", lambda: softmax_cudnn(x)), ("cub", lambda: softmax_cub(x))):
+            try:
+                t = time_flushed(fn)
+                row[label] = {"us": round(t * 1e6, 2),
+                              "frac_hbm": round(nbytes / t / 1e9 / peaks["hbm_gbs"], 4)}
+            except RuntimeError as e:
+                row[label] = {"error": str(e)[:200]}
+        sm[name] = row
+        del x
+    res["softmax"] = sm
+
+    att = {}
+    for B in (64, 2048):
+        s = wl.expert_shape(B)
+        nsets = max(2, min(16, (512 << 20) // wl.attn_bytes(s)))
+        sets = [wl.attn_inputs(s, seed=40 + i) for i in range(nsets)]
+        mask = expert_mask(s)
+        it = [0]
+
+        def sdpa():
+            q, k, v = sets[it[0] % nsets]
+            it[0] += 1
+            return sdpa_gqa_call(q, k, v, mask)
+
+        row = {"input_sets": nsets}
+        try:
+            t = time_calls(sdpa, 20 if B == 2048 else 100)
+            row["torch_sdpa_us"] = round(t * 1e6, 2)
+            row["torch_sdpa_frac_hbm"] = round(wl.attn_bytes(s) / t / 1e9 / peaks["hbm_gbs"], 4)
+        except RuntimeError as e:
+            row["torch_sdpa_error"] = str(e)[:200]
+        it[0] = 0
+
+        def ours():
+            q, k, v = sets[it[0] % nsets]
+            it[0] += 1
+            return fused_attention_gqa_v4(q, k, v, scale=0.125, prefix_len=s.P)
+
+        t = time_calls(ours, 20 if B == 2048 else 100)
+        row["ours_us"] = round(t * 1e6, 2)
+        att[f"C3_B{B}" if B == 64 else "C5_B2048_one_call"] = row
+        del sets
+    # the L2-warm roof: one C3 B=64 input set (36 MB) replayed from a graph
+    s = wl.expert_shape(64)
+    q, k, v = wl.attn_inputs(s, seed=7)
+    tw = time_graph([lambda: fused_attention_gqa_v4(q, k, v, scale=0.125, prefix_len=s.P)] * 32, 10)
+    att["C3_B64_l2_warm"] = {"graph_us": round(tw * 1e6, 2),
+                             "TFLOP/s": round(wl.attn_flops(s) / tw / 1e12, 1),
+                             "tensor_frac": round(wl.attn_flops(s) / tw / 1e12 / peaks["bf16_tflops"], 4),
+                             "note": "one 36 MB input set replayed: K/V/Q stay in L2"}
+    res["attention"] = att
+    res["reference_kernels_sm100a"] = run_ref_kernels_worker()
+    return res
+
+
+def run_ref_kernels_worker(timeout_s: int = 300) -> dict:
+    """Times the reference's own kernels (rebuilt for sm_100a by
+    baseline/build_ref_kernels.py) in a child process."""
+    if not os.path.exists(os.path.join(REF_KERNELS, "manifest.json")):
+        return {"unavailable": "not built (baseline/build_ref_kernels.py needs a reference checkout)"}
+    try:
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--ref-kernels-worker"],
+                           capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"worker exceeded {timeout_s} s"}
+    for line in reversed(r.stdout.splitlines()):
+        if line.startswith("{"):
+            return json.loads(line)
+    return {"unavailable": f"worker rc {r.returncode}: {r.stderr.strip()[-300:]}"}
+
+
+def ref_kernels_worker():
+    """Child process: loads the reference's kernels (their own torch.ops.vlak
+    registrations; this package's libraries are not loaded here) and times
+    softmax versions 1 and 4 on the softmax comparator cases, and the v3 / v4
+    GQA attention at C3 B = 1, 8, 64 (graph replay) and one C5 B=2048 call.
+    A C3 B=8 call is checked against torch SDPA in fp32 (max abs error)."""
+    torch.cuda.set_device(0)
+    man = json.load(open(os.path.join(REF_KERNELS, "manifest.json")))
+    out = {"build": "reference sources unmodified, nvcc -O3 --use_fast_math -gencode "
+                    "arch=compute_100a,code=sm_100a (baseline/build_ref_kernels.py)"}
+    loaded = []
+    for name, st in man.items():
+        if st.get("ok"):
+            torch.ops.load_library(os.path.join(REF_KERNELS, st["so"]))
+            loaded.append(name)
+        else:
+            out[name] = {"unavailable": st.get("error", "not built")}
+    out["loaded"] = loaded
+    peaks, _ = load_peaks()
+    if "vlak_ref_softmax" in loaded:
+        sm = {}
+        for name, shape in SOFTMAX_CMP_CASES:
+            x = _softmax_case(shape)
+            nbytes = wl.softmax_bytes(x.shape[0], x.shape[1], x.element_size())
+            row = {}
+            for ver in (1, 4):
+                t = time_flushed(lambda: torch.ops.vlak.softmax(x, ver))
+                row[f"v{ver}"] = {"us": round(t * 1e6, 2),
+                                  "frac_hbm": round(nbytes / t / 1e9 / peaks["hbm_gbs"], 4)}
+            sm[name] = row
+            del x
+        out["softmax"] = sm
+    ops = []
+    if "vlak_ref_attention" in loaded:
+        ops.append(("v3", torch.ops.vlak.fused_attention_gqa))
+    if "vlak_ref_attention_v4" in loaded:
+        ops.append(("v4", torch.ops.vlak.fused_attention_gqa_v4))
+    att = {}
+    for B in (1, 8, 64):
+        s = wl.expert_shape(B)
+        nsets = max(1, min(64, (256 << 20) // wl.attn_bytes(s)))
+        sets = [wl.attn_inputs(s, seed=10 + i) for i in range(nsets)]
+        row = {"input_sets": nsets}
+        for label, op in ops:
+            tg = time_graph([lambda i=i, op=op: op(*sets[i % nsets], 0.125, s.P, 0, 0)
+                             for i in range(32)])
+            row[f"{label}_graph_us"] = round(tg * 1e6, 2)
+        if B == 8:
+            q, k, v = sets[0]
+            ref = sdpa_gqa_call(q.float(), k.float(), v.float(), expert_mask(s))
+            for label, op in ops:
+                got = op(q, k, v, 0.125, s.P, 0, 0).float().transpose(1, 2)
+                row[f"{label}_max_abs_err_vs_fp32_sdpa"] = float((got - ref).abs().max())
+        att[f"C3_B{B}"] = row
+        del sets
+    s = wl.expert_shape(2048)
+    sets = [wl.attn_inputs(s, seed=60 + i) for i in range(2)]
+    row = {}
+    for label, op in ops:
+        it = [0]
+
+        def call(op=op):
+            q, k, v = sets[it[0] % 2]
+            it[0] += 1
+            op(q, k, v, 0.125, s.P, 0, 0)
+
+        t = time_calls(call, 10, warmup=2)
+        row[f"{label}_us"] = round(t * 1e6, 2)
+        row[f"{label}_frac_hbm"] = round(wl.attn_bytes(s) / t / 1e9 / peaks["hbm_gbs"], 4)
+    att["C5_B2048_one_call"] = row
+    out["attention"] = att
+    print(json.dumps(out), flush=True)
 
 
 def cpu_baseline_sample(target_s: float = 10.0) -> dict:
@@ -616,6 +823,9 @@ def main():
     ap.add_argument("--no-softmax", action="store_true")
     ap.add_argument("--no-sites", action="store_true",
                     help="skip the per-site attention timings (C3, C4, SigLIP)")
+    ap.add_argument("--no-comparators", action="store_true",
+                    help="skip the same-GPU bars (torch, cuDNN, CUB, reference kernels)")
+    ap.add_argument("--ref-kernels-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--case", choices=["attn", "softmax"], default=None,
                     help="profiling mode: a few eager calls of one kernel, no JSON line")
@@ -625,6 +835,9 @@ def main():
     ap.add_argument("--calls", type=int, default=4)
     args = ap.parse_args()
 
+    if args.ref_kernels_worker:
+        ref_kernels_worker()
+        return
     if args.case is not None:
         profile_case(args)
         return

@@ -1,11 +1,13 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Runs in the build container only (it imports the reference's own oracle
-functions from a checkout of djkim9031-research/vla-kernels, by default
-/root/reference, and reads its real-mask fixture). The outputs are small
-.npz files committed beside this script; the tests read only those.
+Runs where a checkout of djkim9031-research/vla-kernels is available: it
+imports the reference's own oracle functions from that checkout and reads its
+real-mask fixture. The checkout's root comes from --reference, else from the
+environment variable VLAK_REFERENCE; there is no default. The outputs are
+small .npz files committed beside this script; the tests read only those.
 
-  python tests/golden/make_golden.py [--reference PATH]
+  python tests/golden/make_golden.py --reference PATH
+  VLAK_REFERENCE=PATH python tests/golden/make_golden.py
 
 Inputs are regenerated from recorded seeds with torch's CPU generator; a
 SHA-256 of the input bytes is stored so a generator change is detected.
@@ -136,8 +138,13 @@ def digest(*tensors) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("VLAK_REFERENCE"),
+                    help="root of a djkim9031-research/vla-kernels checkout "
+                         "(default: $VLAK_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference or not os.path.isfile(os.path.join(a.reference, "tests", "test_attention_gqa.py")):
+        ap.error("give the reference checkout with --reference PATH or VLAK_REFERENCE=PATH "
+                 f"(got {a.reference!r}, which holds no tests/test_attention_gqa.py)")
     sys.path.insert(0, a.reference)
     from tests.test_attention_gqa import ref_attn  # reference oracle
     from vla.variants import _analytic_params      # reference mask solver

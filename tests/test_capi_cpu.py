@@ -24,6 +24,19 @@ def test_library_exports_every_declared_symbol():
     assert all(e.startswith("vlak_") for e in exported), sorted(exported)
 
 
+def test_comparator_library_exports_every_declared_symbol():
+    syms = capi.declared_symbols(capi.CMP_HEADER, "VLAK_CMP_API")
+    assert syms == ["vlak_cmp_last_error_message", "vlak_softmax_cub_fwd",
+                    "vlak_softmax_cudnn_fwd"]
+    L = _native.comparators()
+    for s in syms:
+        assert hasattr(L, s), s
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.CMP_PATH],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == set(syms)
+
+
 def test_abi_version_and_status_strings():
     L = capi.lib()
     assert L.vlak_abi_version() == 1

@@ -4,6 +4,9 @@
                         (nvcc, sm_100a only, static cudart, no torch)
   lib/libvlak_torch.so  torch.ops.vlak schema registration calling the C ABI
                         (g++, torch headers / libraries; no CUDA code)
+  lib/libvlak_comparators.so
+                        library comparators for the softmax benchmark (cuDNN,
+                        CUB), C ABI of include/vlak_comparators.h
 
 Both are rebuilt only when a source is newer than the library. Run directly
 (``python vla-kernels_b200/build.py [--force]``) or through
@@ -25,6 +28,7 @@ INCLUDE = os.path.join(REPO, "include")
 
 CAPI_LIB = os.path.join(LIB_DIR, "libvlak_b200.so")
 TORCH_LIB = os.path.join(LIB_DIR, "libvlak_torch.so")
+CMP_LIB = os.path.join(LIB_DIR, "libvlak_comparators.so")
 
 CU_SOURCES = ["capi.cu", "softmax.cu", "attention_gqa.cu", "attention_simt.cu"]
 HEADERS = ["vlak_device.cuh", "vlak_internal.h"]
@@ -100,8 +104,23 @@ def build_torch_shim(force: bool = False) -> str:
     return TORCH_LIB
 
 
+def build_comparators(force: bool = False) -> str:
+    src = os.path.join(CSRC, "comparators.cu")
+    deps = [src, os.path.join(INCLUDE, "vlak_comparators.h")]
+    if not force and not _stale(CMP_LIB, deps):
+        return CMP_LIB
+    os.makedirs(LIB_DIR, exist_ok=True)
+    nvcc = os.path.join(_cuda_home(), "bin", "nvcc")
+    cmd = [nvcc, *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "--shared",
+           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+           "-I", INCLUDE, "-o", CMP_LIB + ".tmp", src, "-lcudnn"]
+    _run(cmd)
+    os.replace(CMP_LIB + ".tmp", CMP_LIB)
+    return CMP_LIB
+
+
 def build_all(force: bool = False) -> list[str]:
-    return [build_capi(force), build_torch_shim(force)]
+    return [build_capi(force), build_torch_shim(force), build_comparators(force)]
 
 
 if __name__ == "__main__":

@@ -17,10 +17,12 @@ PKG_ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB_DIR = os.path.join(PKG_ROOT, "lib")
 CAPI_PATH = os.path.join(LIB_DIR, "libvlak_b200.so")
 TORCH_PATH = os.path.join(LIB_DIR, "libvlak_torch.so")
+CMP_PATH = os.path.join(LIB_DIR, "libvlak_comparators.so")
 
 _lock = threading.Lock()
 _ops_loaded = False
 _capi = None
+_cmp = None
 
 
 def _require(path: str) -> None:
@@ -55,3 +57,20 @@ def capi() -> ctypes.CDLL:
                 lib.vlak_last_error_message.restype = ctypes.c_char_p
                 _capi = lib
     return _capi
+
+
+def comparators() -> ctypes.CDLL:
+    """The softmax comparator library (include/vlak_comparators.h: cuDNN and
+    CUB row softmax, benchmark bars) through ctypes."""
+    global _cmp
+    if _cmp is None:
+        with _lock:
+            if _cmp is None:
+                _require(CMP_PATH)
+                lib = ctypes.CDLL(CMP_PATH)
+                lib.vlak_cmp_last_error_message.restype = ctypes.c_char_p
+                for f in ("vlak_softmax_cudnn_fwd", "vlak_softmax_cub_fwd"):
+                    getattr(lib, f).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                                ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
+                _cmp = lib
+    return _cmp

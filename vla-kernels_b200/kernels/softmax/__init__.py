@@ -71,14 +71,38 @@ def softmax(x: torch.Tensor, version: str | int = BEST) -> torch.Tensor:
 
 
 # ---- library comparators (cuDNN softmax, CUB-primitive softmax) -------------
-# The reference builds these as a separate extension for benchmarking
-# (kernels/softmax/softmax_baselines.cu). They are not part of this build.
+# Benchmark bars, as in the reference (kernels/softmax/__init__.py:78-114,
+# kernels/softmax/softmax_baselines.cu): not the product path, and not
+# dispatcher ops. They run from lib/libvlak_comparators.so on the current
+# stream.
+
+_CMP_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def _comparator(fn_name: str, x: torch.Tensor) -> torch.Tensor:
+    import ctypes
+
+    if not x.is_cuda or x.dim() != 2:
+        raise RuntimeError("expected a 2D [rows, cols] CUDA tensor")
+    if x.dtype not in _CMP_DTYPES:
+        raise RuntimeError(f"unsupported dtype {x.dtype}")
+    lib = _native.comparators()
+    with torch.cuda.device(x.device):
+        x = x.contiguous()
+        y = torch.empty_like(x)
+        st = getattr(lib, fn_name)(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                                   x.shape[0], x.shape[1], _CMP_DTYPES[x.dtype],
+                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if st != 0:
+        raise RuntimeError(f"{fn_name}: {lib.vlak_cmp_last_error_message().decode()} (status {st})")
+    return y
+
 
 def softmax_cudnn(x: torch.Tensor) -> torch.Tensor:
-    """Vendor comparator (reference: cudnnSoftmaxForward); not built here."""
-    raise RuntimeError("softmax_cudnn comparator is not built in the B200 package")
+    """Vendor comparator: cudnnSoftmaxForward (accurate, per row)."""
+    return _comparator("vlak_softmax_cudnn_fwd", x)
 
 
 def softmax_cub(x: torch.Tensor) -> torch.Tensor:
-    """Library-primitive comparator (reference: cub::BlockReduce); not built here."""
-    raise RuntimeError("softmax_cub comparator is not built in the B200 package")
+    """Library-primitive comparator: block per row, cub::BlockReduce max/sum."""
+    return _comparator("vlak_softmax_cub_fwd", x)
