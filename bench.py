@@ -51,6 +51,8 @@ LAYERS, FLOW_STEPS = 16, 10
 CALLS_PER_STEP = LAYERS * FLOW_STEPS
 METRIC = "GQA attn calls/s (SmolVLA expert self-attn C5, B=2048, 160 calls/chunk; us/call = 1e6/value)"
 UNIT = "calls/s"
+C5_WORKLOAD = ("C5: expert self-attn q(B,50,15,64) k/v(B,291,5,64) P=241, B=2048 "
+               "(sharded over the GPUs, then one NCCL all-gather)")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -270,8 +272,7 @@ def bench_ours(args, rank, world, local):
         "us_per_call": round(1e6 / calls_per_s, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v of the SmolVLA expert shapes)",
-        "config": {"workload": "C5: expert self-attn q(B,50,15,64) k/v(B,291,5,64) P=241, "
-                               "B=2048 sharded over GPUs, 160 calls/step + NCCL all-gather",
+        "config": {"workload": C5_WORKLOAD,
                    "global_batch": GLOBAL_B, "per_gpu_batch": B, "calls_per_step": CALLS_PER_STEP,
                    "parallelism": f"batch-shard x{world}",
                    "l2": "inputs > L2: 16 rotating per-layer input sets, >=144 MB each",
@@ -727,14 +728,13 @@ def ref_kernels_worker():
 
 def cpu_baseline_sample(target_s: float = 10.0) -> dict:
     """The oracle port of the reference's CPU path (torch SDPA, fp32, all host
-    threads) on a bounded sample of C5: B=32 queries per call, as many calls as
-    fit in ~target_s; reported in full-B calls/s."""
+    threads) on the C5 call itself: whole B=2048 calls, as many as fit in
+    ~target_s after one untimed call."""
     from oracle import gqa_attention_torch_cpu
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sample_b = 32
-    s = wl.expert_shape(sample_b)
+    s = wl.expert_shape(GLOBAL_B)
     q, k, v = wl.attn_inputs(s, device="cpu", seed=5)
     gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
     n, t0 = 0, time.perf_counter()
@@ -742,45 +742,44 @@ def cpu_baseline_sample(target_s: float = 10.0) -> dict:
         gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
         n += 1
     dt = time.perf_counter() - t0
-    calls_full = n * sample_b / GLOBAL_B
-    return {"value": round(calls_full / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} calls of B={sample_b} (of 2048) C5 expert self-attn, torch SDPA "
-                      f"fp32 on host, {dt:.1f} s"}
+    return {"value": round(n / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} whole C5 calls (B=2048 expert self-attn), torch SDPA fp32 with "
+                      f"bool mask and repeat_interleave GQA on host, {dt:.1f} s"}
 
 
 # ---------------------------------------------------------------- reference arm
 
 def bench_reference(args, rank, world):
     """The reference's CPU path (torch SDPA with bool mask + repeat_interleave
-    GQA, fp32, all host threads) on the same C5 config, rank 0 only."""
+    GQA, fp32, all host threads) on the same C5 call, rank 0 only: each step
+    is one whole B=2048 call (the unit of the metric), W untimed then K timed."""
     if rank != 0:
         return None
     from oracle import gqa_attention_torch_cpu
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sample_b = 64
-    s = wl.expert_shape(sample_b)
+    s = wl.expert_shape(GLOBAL_B)
     q, k, v = wl.attn_inputs(s, device="cpu", seed=5)
-    for _ in range(args.warmup):
+    for _ in range(max(1, args.warmup)):
         gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         gqa_attention_torch_cpu(q, k, v, s.P, scale=0.125)
     dt = time.perf_counter() - t0
-    value = args.steps * sample_b / GLOBAL_B / dt
+    value = args.steps / dt
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) q/k/v of the SmolVLA expert shapes)",
-        "config": {"workload": "C5: expert self-attn q(B,50,15,64) k/v(B,291,5,64) P=241, "
-                               "B=2048; each step one call on a B=64 sample",
-                   "global_batch": GLOBAL_B, "sample_batch": sample_b,
-                   "parallelism": "host CPU (reference path has no GPU code for sm_100)"},
+        "config": {"workload": C5_WORKLOAD, "global_batch": GLOBAL_B,
+                   "step": "one whole B=2048 call per step",
+                   "parallelism": f"host CPU, {threads} threads (the reference has no sm_100 "
+                                  "code; its CPU path is torch)"},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"B={sample_b} of 2048 per step, torch SDPA fp32"},
+                         "sample": f"{args.steps} whole C5 calls (B=2048), torch SDPA fp32"},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
