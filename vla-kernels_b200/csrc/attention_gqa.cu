@@ -280,30 +280,51 @@ __device__ __forceinline__ Item decode_item(const Params& p, int item) {
   return it;
 }
 
-// Whether key chunk c has a visible key for some row of the item (every role
-// evaluates this identically, so all agree on the item's live chunks). A bool
-// mask is not inspected here: every chunk of its items is processed.
-template <int kMode>
-__device__ __forceinline__ bool chunk_live(const Params& p, const Item& it, int c) {
-  const int c0 = c * kChunk;
-  if (kMode == kMaskBool) return true;
-  if (kMode == kMaskLength) return c0 < it.L && it.m0 < it.L;
-  const int width = min(kChunk, p.N - c0);
-  const int m_hi = min(p.M, it.m0 + it.tiles_active * p.MT) - 1;
-  const int e2_hi = max(p.P, min(p.N, p.N - p.M + m_hi + 1));
-  return (c0 < p.ds) || (c0 + width > p.de && c0 < e2_hi);
-}
-// First live chunk at or after c within the item's split, or -1.
+// The item's live key chunks -- those holding a visible key for some row of
+// the item -- as two intervals [a0, a1) U [b0, b1) (either may be empty).
+// Every role computes them once per item from the same arithmetic, so all
+// roles agree on the chunk sequence; finding the next chunk is then a couple
+// of compares, off the per-chunk critical path of the softmax and MMA warps.
+//  - analytic mask: chunk c is live iff 64c < ds, or its keys reach past de
+//    and it starts before e2_hi (the end of the item's last row's staircase):
+//    [0, ceil(ds / 64)) and [de / 64, ceil(e2_hi / 64)), the second empty when
+//    de >= N (no key lies past de);
+//  - per-sample length L: [0, ceil(L / 64)) when the item's first row is
+//    below L, else nothing;
+//  - bool mask: every chunk (the mask is not inspected here).
+// A split intersects them with its chunk range [c_begin, c_end).
+struct LiveSet {
+  int a0, a1, b0, b1;
+};
 template <int kMode, bool kSplit>
-__device__ __forceinline__ int next_live(const Params& p, const Item& it, int c) {
-  const int end = kSplit ? it.c_end : p.n_chunks;
-  for (; c < end; ++c)
-    if (chunk_live<kMode>(p, it, c)) return c;
+__device__ __forceinline__ LiveSet live_set(const Params& p, const Item& it) {
+  LiveSet s{0, 0, 0, 0};
+  if (kMode == kMaskBool) {
+    s.a1 = p.n_chunks;
+  } else if (kMode == kMaskLength) {
+    s.a1 = it.m0 < it.L ? (it.L + kChunk - 1) / kChunk : 0;
+  } else {
+    s.a1 = min(p.n_chunks, (p.ds + kChunk - 1) / kChunk);
+    if (p.de < p.N) {
+      const int m_hi = min(p.M, it.m0 + it.tiles_active * p.MT) - 1;
+      const int e2_hi = max(p.P, min(p.N, p.N - p.M + m_hi + 1));
+      s.b0 = p.de / kChunk;
+      s.b1 = min(p.n_chunks, (e2_hi + kChunk - 1) / kChunk);
+    }
+  }
+  if (kSplit) {
+    s.a0 = max(s.a0, it.c_begin);
+    s.a1 = min(s.a1, it.c_end);
+    s.b0 = max(s.b0, it.c_begin);
+    s.b1 = min(s.b1, it.c_end);
+  }
+  return s;
+}
+// First live chunk at or after c, or -1.
+__device__ __forceinline__ int live_next(const LiveSet& s, int c) {
+  if (c < s.a1 && s.a0 < s.a1) return max(c, s.a0);
+  if (c < s.b1 && s.b0 < s.b1) return max(c, s.b0);
   return -1;
-}
-template <int kMode, bool kSplit>
-__device__ __forceinline__ int first_live(const Params& p, const Item& it) {
-  return next_live<kMode, kSplit>(p, it, kSplit ? it.c_begin : 0);
 }
 
 // Bits of keys g0 .. g0+31 of one bool-mask row (bit i set when key g0 + i is
@@ -406,9 +427,10 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
     bool ok = true;
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
       const Item it = decode_item<kMode, kSplit>(p, item);
+      const LiveSet ls = live_set<kMode, kSplit>(p, it);
       // an item with no live chunk is written as zeros by the softmax warps
       // alone: no Q, no K/V, no barrier phase
-      if (first_live<kMode, kSplit>(p, it) < 0) continue;
+      if (live_next(ls, 0) < 0) continue;
       // Q buffer qi & 1 is free once the O rows that item qi - 2 staged in
       // it have been stored
       const uint32_t qb = qi & 1;
@@ -431,7 +453,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           tma_load_4d_elect(q_smem + qb * kQBytes + kTileBytes, &p.tm_q, &bars->q_full[qb], 0,
                             it.kvh * p.G, it.m0 + p.MT, it.b);
       }
-      for (int c = first_live<kMode, kSplit>(p, it); c >= 0; c = next_live<kMode, kSplit>(p, it, c + 1)) {
+      for (int c = live_next(ls, 0); c >= 0; c = live_next(ls, c + 1)) {
         const int s = kv % kStages;
         if (!__all_sync(kFullMask, bounded_wait(&bars->kv_empty[s], ((kv / kStages) & 1) ^ 1, abort_flag))) {
           ok = false;
@@ -475,7 +497,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
         const Item it = decode_item<kMode, kSplit>(p, item);
         const bool two = it.tiles_active == 2;
-        if (first_live<kMode, kSplit>(p, it) < 0) continue;  // zeros, written by softmax
+        const LiveSet ls = live_set<kMode, kSplit>(p, it);
+        if (live_next(ls, 0) < 0) continue;  // zeros, written by softmax
         if (!__all_sync(kFullMask, bounded_wait(&bars->q_full[qi & 1], (qi >> 1) & 1, abort_flag))) {
           ok = false;
           break;
@@ -521,7 +544,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
           tc_fence_after();
           return true;
         };
-        int cur = first_live<kMode, kSplit>(p, it);
+        int cur = live_next(ls, 0);
         int j = 0;
         // S of chunk 0 is issued after the previous item's last P.V, which
         // read P from the same columns; tcgen05.mma operations of one thread
@@ -530,7 +553,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
         issue_s(0, cur, 0);
         if (two) issue_s(1, cur, 0);
         while (cur >= 0) {
-          const int nxt = next_live<kMode, kSplit>(p, it, cur + 1);
+          const int nxt = live_next(ls, cur + 1);
           // per tile: P of chunk j ready -> O += P V(j), then S of chunk j+1
           // over the S/P columns (in issue order after the product reading P)
           if (!wait_p(0)) { ok = false; break; }
@@ -602,7 +625,8 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
 
     for (int item = blockIdx.x; ok && item < p.num_items; item += gridDim.x) {
       const Item it = decode_item<kMode, kSplit>(p, item);
-      const bool live = first_live<kMode, kSplit>(p, it) >= 0;
+      const LiveSet ls = live_set<kMode, kSplit>(p, it);
+      const bool live = live_next(ls, 0) >= 0;
       const uint32_t qb = qi & 1;
       qi += live ? 1u : 0u;
       if (pend != 0 && (t >= it.tiles_active || !live)) release();
@@ -642,7 +666,7 @@ gqa_attention_sm100(const __grid_constant__ Params p) {
       }
       float m_run = -INFINITY, l_run = 0.f;
       int j = 0;
-      for (int c = first_live<kMode, kSplit>(p, it); c >= 0; c = next_live<kMode, kSplit>(p, it, c + 1), ++j) {
+      for (int c = live_next(ls, 0); c >= 0; c = live_next(ls, c + 1), ++j) {
         // warp-uniform outcome: the TMEM accesses below are warp-collective
         if (!__all_sync(kFullMask, bounded_wait<kWaitSoftmax>(&bars->s_full[t], sph, abort_flag))) {
           ok = false;
