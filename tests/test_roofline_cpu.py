@@ -64,3 +64,15 @@ def test_cli_prints_both_forms(capsys):
     assert "gqa_attention_sm100" in out and "balanced" in out
     assert roofline.main([LAUNCHES]) == 0
     assert "share" in capsys.readouterr().out
+
+
+def test_short_kernel_names():
+    assert roofline.short("void unnamed>::gqa_attention_sm100<0, 0, 1>(unnamed>::Params)", 60) == \
+        "gqa_attention_sm100<0, 0, 1>"
+    assert roofline.short("void unnamed>::gqa_attention_sm100<0, 0, 1>(unnamed>::Params)", 60,
+                          templates=False) == "gqa_attention_sm100"
+    torch_name = ("void at::native::vectorized_elementwise_kernel<4, at::native::FillFunctor<float>, "
+                  "std::array<char *, 1>>(int, at::native::FillFunctor<float>, std::array<char *, 1>)")
+    assert roofline.short(torch_name, 200, templates=False) == "vectorized_elementwise_kernel"
+    assert roofline.short(torch_name, 29) == "vectorized_elementwise_kernel"
+    assert roofline.short("gemm", 10) == "gemm"

@@ -194,8 +194,37 @@ def kernel_traffic(path: str, kernel_regex: str) -> float | None:
     return statistics.median(vals) if vals else None
 
 
-def short(name: str, width: int) -> str:
-    n = name.split("(")[0].split("::")[-1].strip()
+def _strip_group(n: str, open_ch: str, close_ch: str) -> str:
+    """n without a trailing bracketed group (its matching bracket found by
+    scanning back from the end)."""
+    n = n.rstrip()
+    if not n.endswith(close_ch):
+        return n
+    depth = 0
+    for i in range(len(n) - 1, -1, -1):
+        depth += n[i] == close_ch
+        depth -= n[i] == open_ch
+        if depth == 0:
+            return n[:i]
+    return n
+
+
+def short(name: str, width: int, templates: bool = True) -> str:
+    """A kernel's name without return type, namespaces or parameter list, and
+    without its template arguments unless `templates`:
+    "void ns::k<float, 4>(int)" -> "k<float, 4>" (or "k")."""
+    n = _strip_group(name, "(", ")")
+    if not templates:
+        n = _strip_group(n, "<", ">")
+    depth, cut = 0, 0  # the last "::" outside template brackets
+    for i, ch in enumerate(n):
+        depth += ch == "<"
+        depth -= ch == ">" and depth > 0
+        if depth == 0 and n.startswith("::", i):
+            cut = i + 2
+    n = n[cut:].strip()
+    if n.startswith("void "):
+        n = n[5:]
     return (n or name)[:width]
 
 
@@ -239,4 +268,7 @@ def main(argv=None):
 
 
 if __name__ == "__main__":
-    sys.exit(main())
+    try:
+        sys.exit(main())
+    except BrokenPipeError:  # output piped into head and the like
+        sys.exit(0)
