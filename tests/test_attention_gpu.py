@@ -145,6 +145,10 @@ NARROW = [
     (1, 19, 77, 8, 1, 50, 10, 20),       # G=8: 24 rows
     (2, 30, 64, 5, 1, 64, 0, 0),         # G=5: 25 rows
     (96, 50, 291, 15, 5, 241, 196, 240),  # C3 with the real dead band, unsplit
+    (2, 43, 100, 15, 5, 80, 0, 0),       # G=3: tile 1 holds one position (3 rows)
+    (2, 52, 291, 15, 5, 241, 196, 240),  # G=3: 10 positions, 30 rows (the most for G=3)
+    (1, 10, 130, 16, 1, 100, 30, 70),    # G=16: 2 positions, exactly 32 rows
+    (3, 160, 161, 2, 2, 161, 0, 0),      # G=1: 32 rows, a one-key last chunk
 ]
 
 
